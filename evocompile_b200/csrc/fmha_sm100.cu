@@ -1,0 +1,605 @@
+// Fused multi-head attention forward for sm_100a (gko::fused_sdpa_pair,
+// gko::cutlass_fmha_pair, gko::fmha_varlen_fwd).
+//
+// One CTA computes a 128-row query tile of one (batch, head) against the key
+// range its masks allow, in 128-key tiles:
+//   warp 0     TMA producer: Q once, then K_j / V_j into a 2-stage ring
+//   warp 1     MMA issuer + TMEM owner: S_j = Q K_j^T into TMEM (2 buffers),
+//              O += P_j V_j into a TMEM accumulator
+//   warps 2-5  softmax: one thread per query row reads S_j from TMEM, applies
+//              scale / bias / softcap / masks, keeps the running max and sum,
+//              writes P_j (bf16/f16) to shared memory, rescales O in TMEM only
+//              when the running max grows by more than 2^8, and finally
+//              normalises O and writes out / lse.
+// Semantics follow the reference Triton kernel _flash_fwd
+// (eval/kernels/fused_sdpa.py:25-157): logits = scale * q.k (+ bias), then
+// softcap, then masks (key padding, causal key <= query, |key - query| <= window);
+// lse = max + ln(sum). GQA maps query head h to kv head h / (hq / hkv).
+#include <type_traits>
+
+#include "host_common.h"
+#include "sm100_ptx.cuh"
+
+namespace gko {
+namespace fmha {
+
+constexpr int kBM = 128;
+constexpr int kBN = 128;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr float kRescaleThreshold = 8.f;  // log2 units
+
+struct Params {
+  int hq, hkv, group;  // group = hq / hkv
+  int sq, sk;          // dense: per-batch lengths; varlen: unused
+  int q_tiles;         // tiles along the query axis (grid.y)
+  float scale, scale_log2, softcap;
+  int causal, window;
+  // bias (dense only)
+  const void* bias;
+  int bias_mode, bias_dtype, bias_z;  // batch index = z % bias_z
+  int64_t b_sz, b_sh, b_sq, b_sk;
+  // outputs
+  void* out;
+  float* lse;
+  int64_t lse_stride_h;  // dense: sq (rows of one head); varlen: total tokens
+  const int* cu_q;
+  const int* cu_k;
+  int total_q;  // varlen: tq
+  unsigned* status;
+};
+
+template <int D>
+struct Layout {
+  static constexpr uint32_t kChunk = 128 * 128;  // one [128 rows x 128 B] swizzle block
+  static constexpr int kChunks = D / 64;
+  static constexpr uint32_t kTile = kChunks * kChunk;  // 128 x D elements
+  static constexpr uint32_t kQ = 0;
+  static constexpr uint32_t kK0 = kQ + kTile;
+  static constexpr uint32_t kV0 = kK0 + 2 * kTile;
+  static constexpr uint32_t kP = kV0 + 2 * kTile;
+  static constexpr uint32_t kMeta = kP + 2 * kChunk;
+  // at least 120 KB so that a single CTA (and its 512 TMEM columns) occupies an SM
+  static constexpr uint32_t kBytes = (1024 + kMeta + 256) > 122880 ? (1024 + kMeta + 256) : 122880;
+};
+
+__device__ __forceinline__ float bias_value(const Params& p, int z, int h, int q, int k) {
+  const int64_t off = (int64_t)(z % p.bias_z) * p.b_sz + (int64_t)h * p.b_sh + (int64_t)q * p.b_sq +
+                      (int64_t)k * p.b_sk;
+  if (p.bias_dtype == GKO_F32) return __ldg(reinterpret_cast<const float*>(p.bias) + off);
+  if (p.bias_dtype == GKO_BF16)
+    return __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16*>(p.bias) + off));
+  return __half2float(__ldg(reinterpret_cast<const __half*>(p.bias) + off));
+}
+
+template <typename T, int D, bool VARLEN, bool EXTRA>
+__global__ void __launch_bounds__(kThreads, 1)
+    fmha_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  using L = Layout<D>;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t kIdescS = make_idesc_f16(kBF16, kBM, kBN, false, false);
+  constexpr uint32_t kIdescO = make_idesc_f16(kBF16, kBM, D, false, true);
+
+  // ---------------------------------------------------------- tile geometry
+  const int bh = blockIdx.x;
+  const int h = bh % p.hq;
+  const int zb = bh / p.hq;  // batch (dense) or sequence (varlen)
+  const int qt = p.q_tiles - 1 - (int)blockIdx.y;  // heaviest (causal) tiles first
+  const int m0 = qt * kBM;
+  int len_q, len_k, row_q0, row_k0;
+  if constexpr (VARLEN) {
+    row_q0 = p.cu_q[zb];
+    len_q = p.cu_q[zb + 1] - row_q0;
+    row_k0 = p.cu_k[zb];
+    len_k = p.cu_k[zb + 1] - row_k0;
+  } else {
+    row_q0 = 0;
+    len_q = p.sq;
+    row_k0 = 0;
+    len_k = p.sk;
+  }
+  if (m0 >= len_q) return;  // uniform across the CTA, before any barrier or TMEM use
+  const int hk = h / p.group;
+  const int zc = VARLEN ? 0 : zb;  // tensor-map batch coordinate
+
+  // key range this query tile can see
+  int k_lo = 0, k_hi = len_k;
+  if (p.causal) k_hi = min(k_hi, m0 + kBM);
+  if (p.window > 0) {
+    k_lo = max(k_lo, m0 - p.window);
+    k_hi = min(k_hi, m0 + kBM + p.window);
+  }
+  const int t_lo = k_lo / kBN;
+  const int n_tiles = (k_hi > k_lo) ? ((k_hi + kBN - 1) / kBN - t_lo) : 0;
+
+  // ---------------------------------------------------------- shared memory
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
+  const uint32_t sb = raw_addr + pad;
+  uint8_t* meta = smem_raw + pad + L::kMeta;
+  const uint32_t smeta = sb + L::kMeta;
+  const uint32_t bar_q = smeta;
+  const uint32_t bar_kfull = smeta + 8;    // [2]
+  const uint32_t bar_kempty = smeta + 24;  // [2]
+  const uint32_t bar_vfull = smeta + 40;   // [2]
+  const uint32_t bar_vempty = smeta + 56;  // [2]
+  const uint32_t bar_sfull = smeta + 72;   // [2]
+  const uint32_t bar_sfree = smeta + 88;   // [2]
+  const uint32_t bar_pfull = smeta + 104;
+  const uint32_t bar_odone = smeta + 112;
+  const uint32_t bar_drain = smeta + 120;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 128);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 132);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_q, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_kfull + 8 * i, 1);
+      mbar_init(bar_kempty + 8 * i, 1);
+      mbar_init(bar_vfull + 8 * i, 1);
+      mbar_init(bar_vempty + 8 * i, 1);
+      mbar_init(bar_sfull + 8 * i, 1);
+      mbar_init(bar_sfree + 8 * i, 4);
+    }
+    mbar_init(bar_pfull, 4);
+    mbar_init(bar_odone, 1);
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_o = tmem_base + 256;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && n_tiles > 0) {
+      mbar_arrive_expect_tx(bar_q, L::kTile);
+#pragma unroll
+      for (int c = 0; c < L::kChunks; ++c)
+        tma_load_4d(sb + L::kQ + c * L::kChunk, &tm_q, bar_q, c * 64, row_q0 + m0, h, zc);
+      for (int i = 0; i < n_tiles; ++i) {
+        const int st = i & 1;
+        const uint32_t ph = (i >> 1) & 1;
+        const int krow = row_k0 + (t_lo + i) * kBN;
+        if (!wait_bounded(bar_kempty + 8 * st, ph ^ 1, abort_flag, p.status, kStatusTimeoutProducer))
+          break;
+        mbar_arrive_expect_tx(bar_kfull + 8 * st, L::kTile);
+#pragma unroll
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_4d(sb + L::kK0 + st * L::kTile + c * L::kChunk, &tm_k, bar_kfull + 8 * st, c * 64,
+                      krow, hk, zc);
+        if (!wait_bounded(bar_vempty + 8 * st, ph ^ 1, abort_flag, p.status, kStatusTimeoutProducer))
+          break;
+        mbar_arrive_expect_tx(bar_vfull + 8 * st, L::kTile);
+#pragma unroll
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_4d(sb + L::kV0 + st * L::kTile + c * L::kChunk, &tm_v, bar_vfull + 8 * st, c * 64,
+                      krow, hk, zc);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && n_tiles > 0) {
+      bool ok = wait_bounded(bar_q, 0, abort_flag, p.status, kStatusTimeoutMma);
+      auto issue_pv = [&](int i) -> bool {
+        const int st = i & 1;
+        if (!wait_bounded(bar_pfull, i & 1, abort_flag, p.status, kStatusTimeoutMma)) return false;
+        if (!wait_bounded(bar_vfull + 8 * st, (i >> 1) & 1, abort_flag, p.status, kStatusTimeoutMma))
+          return false;
+        tc_fence_after();
+        const uint32_t v_addr = sb + L::kV0 + st * L::kTile;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint64_t adesc =
+              make_sdesc_sw128(sb + L::kP + (kk >> 2) * L::kChunk + (kk & 3) * 32, 16, 1024);
+          const uint64_t bdesc = make_sdesc_sw128(v_addr + kk * 16 * 128, L::kChunk, 1024);
+          mma_f16_ss(tmem_o, adesc, bdesc, kIdescO, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(bar_odone);
+        mma_commit(bar_vempty + 8 * st);
+        return true;
+      };
+      for (int i = 0; i < n_tiles && ok; ++i) {
+        const int st = i & 1;
+        if (!wait_bounded(bar_kfull + 8 * st, (i >> 1) & 1, abort_flag, p.status, kStatusTimeoutMma) ||
+            !wait_bounded(bar_sfree + 8 * st, ((i >> 1) & 1) ^ 1, abort_flag, p.status,
+                          kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k_addr = sb + L::kK0 + st * L::kTile;
+        const uint32_t s_tmem = tmem_base + st * kBN;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
+          const uint64_t adesc = make_sdesc_sw128(sb + L::kQ + off, 16, 1024);
+          const uint64_t bdesc = make_sdesc_sw128(k_addr + off, 16, 1024);
+          mma_f16_ss(s_tmem, adesc, bdesc, kIdescS, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar_sfull + 8 * st);
+        mma_commit(bar_kempty + 8 * st);
+        if (i >= 1 && !issue_pv(i - 1)) ok = false;
+      }
+      if (ok) ok = issue_pv(n_tiles - 1);
+      if (*abort_flag) {
+        mma_commit(bar_drain);
+        wait_for(bar_drain, 0, p.status, kStatusTimeoutDrain);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax / epilogue
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // query row within the tile
+    const int qi = m0 + r;              // query index within the sequence
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    float m_run = -INFINITY;  // running max, log2 domain
+    float l_run = 0.f;
+    bool ok = true;
+    for (int i = 0; i < n_tiles; ++i) {
+      const int st = i & 1;
+      const int kbase = (t_lo + i) * kBN;
+      if (!wait_bounded(bar_sfull + 8 * st, (i >> 1) & 1, abort_flag, p.status,
+                        kStatusTimeoutSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[kBN];
+      {
+        uint32_t su[kBN];
+#pragma unroll
+        for (int c = 0; c < kBN / 32; ++c) tmem_ld32p(tmem_base + lane_off + st * kBN + c * 32, su + c * 32);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) s[c] = __uint_as_float(su[c]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_sfree + 8 * st);
+
+      // logits in the log2 domain
+      const bool need_mask = (kbase + kBN > len_k) || (p.causal && kbase + kBN - 1 > m0);
+      float tmax = -INFINITY;
+      if constexpr (EXTRA) {
+#pragma unroll
+        for (int c = 0; c < kBN; ++c) {
+          const int kj = kbase + c;
+          float t = s[c] * p.scale;
+          if (p.bias_mode != GKO_BIAS_NONE && kj < len_k && qi < len_q) t += bias_value(p, zb, h, qi, kj);
+          if (p.softcap > 0.f) {
+            float x = fminf(fmaxf(t / p.softcap, -15.f), 15.f);
+            t = p.softcap * tanhf(x);
+          }
+          bool keep = kj < len_k;
+          if (p.causal) keep = keep && (kj <= qi);
+          if (p.window > 0) keep = keep && (kj - qi <= p.window) && (qi - kj <= p.window);
+          s[c] = keep ? t * kLog2e : -INFINITY;
+          tmax = fmaxf(tmax, s[c]);
+        }
+      } else {
+        if (need_mask) {
+#pragma unroll
+          for (int c = 0; c < kBN; ++c) {
+            const int kj = kbase + c;
+            bool keep = kj < len_k;
+            if (p.causal) keep = keep && (kj <= qi);
+            s[c] = keep ? s[c] * p.scale_log2 : -INFINITY;
+            tmax = fmaxf(tmax, s[c]);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < kBN; ++c) {
+            s[c] *= p.scale_log2;
+            tmax = fmaxf(tmax, s[c]);
+          }
+        }
+      }
+      // lazy rescale: keep the old max unless the new one exceeds it by the threshold
+      float m_new = m_run;
+      float alpha = 1.f;
+      if (tmax > m_run + kRescaleThreshold || (m_run == -INFINITY && tmax > -INFINITY)) {
+        m_new = tmax;
+        alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
+      }
+      const float m_sub = (m_new == -INFINITY) ? 0.f : m_new;
+      float rsum = 0.f;
+      uint32_t pk[kBN / 2];
+#pragma unroll
+      for (int c = 0; c < kBN / 2; ++c) {
+        const float p0 = fast_exp2(s[2 * c] - m_sub);
+        const float p1 = fast_exp2(s[2 * c + 1] - m_sub);
+        rsum += p0 + p1;
+        pk[c] = Cvt<T>::pack(p0, p1);
+      }
+      // P buffer and O are free once PV_{i-1} has completed
+      if (i > 0) {
+        if (!wait_bounded(bar_odone, (i - 1) & 1, abort_flag, p.status, kStatusTimeoutSoftmax)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tmem_o + lane_off + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tmem_o + lane_off + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P tile (128 rows x 128 keys), K-major, 128-byte swizzle, two 64-key chunks
+#pragma unroll
+      for (int j = 0; j < kBN / 8; ++j) {
+        const int chunk = j >> 3;
+        const int piece = j & 7;
+        const uint32_t addr =
+            sb + L::kP + chunk * L::kChunk + r * 128 + ((piece ^ (r & 7)) << 4);
+        st_shared_v4(addr, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_pfull);
+      l_run = l_run * alpha + rsum;
+      m_run = m_new;
+    }
+
+    // ---------------------------------------------------------- epilogue
+    if (ok && n_tiles > 0) {
+      ok = wait_bounded(bar_odone, (n_tiles - 1) & 1, abort_flag, p.status, kStatusTimeoutSoftmax);
+      tc_fence_after();
+    }
+    const bool write = qi < len_q;
+    T* orow;
+    if constexpr (VARLEN)
+      orow = reinterpret_cast<T*>(p.out) + ((int64_t)(row_q0 + qi) * p.hq + h) * D;
+    else
+      orow = reinterpret_cast<T*>(p.out) + (((int64_t)zb * p.hq + h) * p.sq + qi) * D;
+    const float inv = (l_run > 0.f) ? 1.f / l_run : 0.f;
+    if (ok && n_tiles > 0) {
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tmem_o + lane_off + c * 32, o);
+        tmem_wait_ld();
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          w[e] = Cvt<T>::pack(__uint_as_float(o[2 * e]) * inv, __uint_as_float(o[2 * e + 1]) * inv);
+        if (write) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+        }
+      }
+    } else if (write) {
+      uint4* dst = reinterpret_cast<uint4*>(orow);
+#pragma unroll
+      for (int e = 0; e < D / 8; ++e) dst[e] = make_uint4(0, 0, 0, 0);
+    }
+    if (write) {
+      const float lse = (l_run > 0.f) ? (m_run + log2f(l_run)) * kLn2 : -INFINITY;
+      if constexpr (VARLEN)
+        p.lse[(int64_t)h * p.lse_stride_h + row_q0 + qi] = lse;
+      else
+        p.lse[((int64_t)zb * p.hq + h) * p.lse_stride_h + qi] = lse;
+    }
+    tc_fence_before();
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+// ------------------------------------------------------------------ host side
+template <typename T, int D, bool VARLEN, bool EXTRA>
+int launch(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const Params& p,
+           dim3 grid, cudaStream_t s) {
+  auto kern = fmha_fwd_kernel<T, D, VARLEN, EXTRA>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout<D>::kBytes);
+    if (e != cudaSuccess) return host::cuda_check(e, "cudaFuncSetAttribute(fmha)");
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  kern<<<grid, kThreads, Layout<D>::kBytes, s>>>(tq, tk, tv, p);
+  return host::cuda_check(cudaGetLastError(), "fmha kernel launch");
+}
+
+template <typename T, bool VARLEN>
+int dispatch(int d, bool extra, const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+             const Params& p, dim3 grid, cudaStream_t s) {
+  if (d == 64)
+    return extra ? launch<T, 64, VARLEN, true>(tq, tk, tv, p, grid, s)
+                 : launch<T, 64, VARLEN, false>(tq, tk, tv, p, grid, s);
+  return extra ? launch<T, 128, VARLEN, true>(tq, tk, tv, p, grid, s)
+               : launch<T, 128, VARLEN, false>(tq, tk, tv, p, grid, s);
+}
+
+// 4-D tensor map over (d, s, h, z) for one operand; strides in elements for (z, h, s).
+bool make_map(CUtensorMap* m, int dtype, const void* base, int64_t z, int64_t h, int64_t s, int64_t d,
+              int64_t sz, int64_t sh, int64_t ss) {
+  uint64_t dims[4] = {(uint64_t)d, (uint64_t)s, (uint64_t)h, (uint64_t)z};
+  uint64_t str[3] = {(uint64_t)ss * 2, (uint64_t)sh * 2, (uint64_t)sz * 2};
+  uint32_t box[4] = {64, 128, 1, 1};
+  return host::encode_tmap(m, dtype, 4, base, dims, str, box);
+}
+
+int check_common(int dtype, int64_t hq, int64_t hkv, int64_t d, float scale, int window, float softcap) {
+  using host::fail;
+  if (dtype != GKO_F16 && dtype != GKO_BF16)
+    return fail(GKO_ERR_UNSUPPORTED, "fmha supports float16 and bfloat16 only (dtype code %d)", dtype);
+  if (d != 64 && d != 128)
+    return fail(GKO_ERR_UNSUPPORTED, "fmha supports head dim 64 or 128, got %lld", (long long)d);
+  if (hq <= 0 || hkv <= 0 || hq % hkv)
+    return fail(GKO_ERR_INVALID, "query heads (%lld) must be a positive multiple of kv heads (%lld)",
+                (long long)hq, (long long)hkv);
+  if (window < 0) return fail(GKO_ERR_INVALID, "window must be >= 0");
+  if (!(softcap >= 0.f)) return fail(GKO_ERR_INVALID, "softcap must be >= 0");
+  if (!(scale == scale)) return fail(GKO_ERR_INVALID, "scale is NaN");
+  return GKO_OK;
+}
+
+}  // namespace fmha
+}  // namespace gko
+
+using namespace gko;
+using gko::host::fail;
+
+extern "C" int gko_fmha_fwd(int dtype, int64_t z, int64_t hq, int64_t hkv, int64_t sq, int64_t sk,
+                            int64_t d, const void* q, const int64_t* qs, const void* k,
+                            const int64_t* ks, const void* v, const int64_t* vs, const void* bias,
+                            int bias_mode, int bias_dtype, const int64_t* bs, int64_t bias_batch,
+                            float scale,
+                            int causal, int window, float softcap, void* out, float* lse,
+                            unsigned int* status, void* stream) {
+  int rc = fmha::check_common(dtype, hq, hkv, d, scale, window, softcap);
+  if (rc) return rc;
+  if (z < 0 || sq < 0 || sk < 0) return fail(GKO_ERR_INVALID, "negative attention size");
+  if (z == 0 || sq == 0) return GKO_OK;
+  if (!q || !k || !v || !out || !lse || !qs || !ks || !vs)
+    return fail(GKO_ERR_INVALID, "null pointer argument");
+  if (qs[3] != 1 || ks[3] != 1 || vs[3] != 1)
+    return fail(GKO_ERR_UNSUPPORTED, "fmha needs unit stride along the head dim");
+  for (int i = 0; i < 3; ++i)
+    if (qs[i] % 8 || ks[i] % 8 || vs[i] % 8 || qs[i] < 0 || ks[i] < 0 || vs[i] < 0)
+      return fail(GKO_ERR_UNSUPPORTED,
+                  "fmha needs non-negative q/k/v strides that are multiples of 8 elements");
+  if (!host::aligned16(q) || !host::aligned16(k) || !host::aligned16(v) || !host::aligned16(out))
+    return fail(GKO_ERR_UNSUPPORTED, "fmha needs 16-byte aligned q, k, v, out");
+  if (sq > (1 << 30) || sk > (1 << 30) || z * hq >= (1ll << 31))
+    return fail(GKO_ERR_UNSUPPORTED, "fmha sizes out of range");
+  if (bias_mode != GKO_BIAS_NONE && bias_mode != GKO_BIAS_KEYPAD && bias_mode != GKO_BIAS_FULL)
+    return fail(GKO_ERR_INVALID, "unknown bias mode %d", bias_mode);
+  if (bias_mode != GKO_BIAS_NONE) {
+    if (!bias || !bs) return fail(GKO_ERR_INVALID, "bias mode set but bias pointer is null");
+    if (bias_dtype != GKO_F16 && bias_dtype != GKO_BF16 && bias_dtype != GKO_F32)
+      return fail(GKO_ERR_INVALID, "unknown bias dtype %d", bias_dtype);
+  }
+  CUtensorMap tq, tk, tv;
+  if (!fmha::make_map(&tq, dtype, q, z, hq, sq, d, qs[0], qs[1], qs[2]) ||
+      !fmha::make_map(&tk, dtype, k, z, hkv, sk > 0 ? sk : 1, d, ks[0], ks[1], ks[2]) ||
+      !fmha::make_map(&tv, dtype, v, z, hkv, sk > 0 ? sk : 1, d, vs[0], vs[1], vs[2]))
+    return GKO_ERR_INVALID;
+  fmha::Params p{};
+  p.hq = (int)hq;
+  p.hkv = (int)hkv;
+  p.group = (int)(hq / hkv);
+  p.sq = (int)sq;
+  p.sk = (int)sk;
+  p.q_tiles = (int)((sq + fmha::kBM - 1) / fmha::kBM);
+  p.scale = scale;
+  p.scale_log2 = scale * fmha::kLog2e;
+  p.softcap = softcap;
+  p.causal = causal ? 1 : 0;
+  p.window = window;
+  p.bias = bias;
+  p.bias_mode = bias_mode;
+  p.bias_dtype = bias_dtype;
+  p.bias_z = 1;
+  if (bias_mode == GKO_BIAS_KEYPAD) {
+    p.b_sz = bs[0];
+    p.b_sh = 0;
+    p.b_sq = 0;
+    p.b_sk = bs[3];
+  } else if (bias_mode == GKO_BIAS_FULL) {
+    p.b_sz = bs[0];
+    p.b_sh = bs[1];
+    p.b_sq = bs[2];
+    p.b_sk = bs[3];
+  }
+  if (bias_mode != GKO_BIAS_NONE) {
+    if (bias_batch <= 0 || bias_batch > z || z % bias_batch)
+      return fail(GKO_ERR_INVALID, "bias batch count %lld must divide the batch %lld",
+                  (long long)bias_batch, (long long)z);
+    p.bias_z = (int)bias_batch;
+  }
+  p.out = out;
+  p.lse = lse;
+  p.lse_stride_h = sq;
+  p.status = status;
+  const bool extra = bias_mode != GKO_BIAS_NONE || softcap > 0.f || window > 0;
+  dim3 grid((unsigned)(z * hq), (unsigned)p.q_tiles);
+  if (grid.y > 65535) return fail(GKO_ERR_UNSUPPORTED, "fmha supports sq <= 8388480");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == GKO_BF16) return fmha::dispatch<__nv_bfloat16, false>((int)d, extra, tq, tk, tv, p, grid, s);
+  return fmha::dispatch<__half, false>((int)d, extra, tq, tk, tv, p, grid, s);
+}
+
+extern "C" int gko_fmha_varlen_fwd(int dtype, int64_t b, int64_t hq, int64_t hkv, int64_t d,
+                                   int64_t tq, int64_t tk, int64_t max_seqlen_q, const void* q,
+                                   int64_t q_st, int64_t q_sh, const void* k, int64_t k_st,
+                                   int64_t k_sh, const void* v, int64_t v_st, int64_t v_sh,
+                                   const int32_t* cu_q, const int32_t* cu_k, float scale, int causal,
+                                   int window, float softcap, void* out, float* lse,
+                                   unsigned int* status, void* stream) {
+  int rc = fmha::check_common(dtype, hq, hkv, d, scale, window, softcap);
+  if (rc) return rc;
+  if (b < 0 || tq < 0 || tk < 0 || max_seqlen_q < 0) return fail(GKO_ERR_INVALID, "negative size");
+  if (b == 0 || tq == 0 || max_seqlen_q == 0) return GKO_OK;
+  if (!q || !k || !v || !out || !lse || !cu_q || !cu_k)
+    return fail(GKO_ERR_INVALID, "null pointer argument");
+  if (q_st % 8 || q_sh % 8 || k_st % 8 || k_sh % 8 || v_st % 8 || v_sh % 8)
+    return fail(GKO_ERR_UNSUPPORTED, "fmha needs token/head strides that are multiples of 8");
+  if (!host::aligned16(q) || !host::aligned16(k) || !host::aligned16(v) || !host::aligned16(out))
+    return fail(GKO_ERR_UNSUPPORTED, "fmha needs 16-byte aligned q, k, v, out");
+  if (tq >= (1ll << 31) || tk >= (1ll << 31)) return fail(GKO_ERR_UNSUPPORTED, "too many tokens");
+  CUtensorMap mq, mk, mv;
+  if (!fmha::make_map(&mq, dtype, q, 1, hq, tq, d, tq * q_st, q_sh, q_st) ||
+      !fmha::make_map(&mk, dtype, k, 1, hkv, tk > 0 ? tk : 1, d, tk * k_st, k_sh, k_st) ||
+      !fmha::make_map(&mv, dtype, v, 1, hkv, tk > 0 ? tk : 1, d, tk * v_st, v_sh, v_st))
+    return GKO_ERR_INVALID;
+  fmha::Params p{};
+  p.hq = (int)hq;
+  p.hkv = (int)hkv;
+  p.group = (int)(hq / hkv);
+  p.q_tiles = (int)((max_seqlen_q + fmha::kBM - 1) / fmha::kBM);
+  p.scale = scale;
+  p.scale_log2 = scale * fmha::kLog2e;
+  p.softcap = softcap;
+  p.causal = causal ? 1 : 0;
+  p.window = window;
+  p.bias_mode = GKO_BIAS_NONE;
+  p.bias_z = 1;
+  p.out = out;
+  p.lse = lse;
+  p.lse_stride_h = tq;
+  p.cu_q = cu_q;
+  p.cu_k = cu_k;
+  p.total_q = (int)tq;
+  p.status = status;
+  const bool extra = softcap > 0.f || window > 0;
+  dim3 grid((unsigned)(b * hq), (unsigned)p.q_tiles);
+  if (grid.y > 65535) return fail(GKO_ERR_UNSUPPORTED, "fmha supports max_seqlen_q <= 8388480");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == GKO_BF16) return fmha::dispatch<__nv_bfloat16, true>((int)d, extra, mq, mk, mv, p, grid, s);
+  return fmha::dispatch<__half, true>((int)d, extra, mq, mk, mv, p, grid, s);
+}

@@ -1,0 +1,215 @@
+// C-ABI entry points for the fused GEMM operators (gko_addmm_act, gko_linear_swiglu).
+#include "gemm_f32.cuh"
+#include "gemm_sm100.cuh"
+#include "host_common.h"
+
+using namespace gko;
+using gko::host::fail;
+
+namespace {
+
+int bias_kind_of(const void* bias, int bias_dtype) {
+  if (!bias) return kBiasNone;
+  switch (bias_dtype) {
+    case GKO_F16: return kBiasF16;
+    case GKO_BF16: return kBiasBF16;
+    case GKO_F32: return kBiasF32;
+    default: return -1;
+  }
+}
+
+template <typename T, int EPI, bool B_MN>
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
+              const GemmParams& p, cudaStream_t stream) {
+  auto kern = gemm::gemm_kernel<T, EPI, B_MN>;
+  static bool configured[64] = {false};  // per instantiation and device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         gemm::kSmemBytes);
+    if (e != cudaSuccess) return host::cuda_check(e, "cudaFuncSetAttribute(gemm)");
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  const int grid = p.num_tiles < host::sm_count() ? p.num_tiles : host::sm_count();
+  kern<<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(ta, tb, td, p);
+  return host::cuda_check(cudaGetLastError(), "gemm kernel launch");
+}
+
+template <typename T>
+int dispatch_tc(int epi, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
+                const CUtensorMap& td, const GemmParams& p, cudaStream_t s) {
+  if (!b_mn) {
+    switch (epi) {
+      case kEpiNone: return launch_tc<T, kEpiNone, false>(ta, tb, td, p, s);
+      case kEpiGelu: return launch_tc<T, kEpiGelu, false>(ta, tb, td, p, s);
+      case kEpiRelu: return launch_tc<T, kEpiRelu, false>(ta, tb, td, p, s);
+      default: return launch_tc<T, kEpiSwiglu, false>(ta, tb, td, p, s);
+    }
+  }
+  switch (epi) {
+    case kEpiNone: return launch_tc<T, kEpiNone, true>(ta, tb, td, p, s);
+    case kEpiGelu: return launch_tc<T, kEpiGelu, true>(ta, tb, td, p, s);
+    case kEpiRelu: return launch_tc<T, kEpiRelu, true>(ta, tb, td, p, s);
+    default: return launch_tc<T, kEpiSwiglu, true>(ta, tb, td, p, s);
+  }
+}
+
+// Tensor-core path. A: [M, K] row stride lda. B storage: K-major [nb_rows, K] row stride ldb
+// (b_mn = false) or MN-major [K, nb_cols] row stride ldb (b_mn = true), where the logical
+// B rows (output columns, SwiGLU: gate then up) number nb_total. D: [M, N_out] row stride ldd.
+int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_total,
+           int64_t up_offset, const void* a, int64_t lda, const void* b, int64_t ldb, bool b_mn,
+           const void* bias, int bias_kind, void* d, int64_t ldd, unsigned* status,
+           cudaStream_t stream) {
+  if (!host::aligned16(a) || !host::aligned16(b) || !host::aligned16(d))
+    return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs 16-byte aligned operand bases");
+  if (lda % 8 || ldb % 8 || ldd % 8)
+    return fail(GKO_ERR_UNSUPPORTED,
+                "tensor-core GEMM needs row strides that are multiples of 8 elements "
+                "(lda=%lld ldb=%lld ldd=%lld)",
+                (long long)lda, (long long)ldb, (long long)ldd);
+  if (K % 8 || N_out % 8)
+    return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs K %% 8 == 0 and N %% 8 == 0 "
+                "(K=%lld N=%lld)", (long long)K, (long long)N_out);
+  if (b_mn && epi == kEpiSwiglu && up_offset % 8)
+    return fail(GKO_ERR_UNSUPPORTED, "transposed SwiGLU weight needs h %% 8 == 0");
+  if (M >= (1ll << 31) || N_out >= (1ll << 31) || K >= (1ll << 31))
+    return fail(GKO_ERR_UNSUPPORTED, "GEMM dimensions must be < 2^31");
+  const int esz = 2;
+  CUtensorMap ta, tb, td;
+  {
+    uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
+    uint64_t str[1] = {(uint64_t)(lda * esz)};
+    uint32_t box[2] = {64, 128};
+    if (!host::encode_tmap(&ta, dtype, 2, a, dims, str, box)) return GKO_ERR_INVALID;
+  }
+  if (!b_mn) {
+    uint64_t dims[2] = {(uint64_t)K, (uint64_t)nb_total};
+    uint64_t str[1] = {(uint64_t)(ldb * esz)};
+    uint32_t box[2] = {64, 128};
+    if (!host::encode_tmap(&tb, dtype, 2, b, dims, str, box)) return GKO_ERR_INVALID;
+  } else {
+    uint64_t dims[2] = {(uint64_t)nb_total, (uint64_t)K};
+    uint64_t str[1] = {(uint64_t)(ldb * esz)};
+    uint32_t box[2] = {64, 64};
+    if (!host::encode_tmap(&tb, dtype, 2, b, dims, str, box)) return GKO_ERR_INVALID;
+  }
+  {
+    uint64_t dims[2] = {(uint64_t)N_out, (uint64_t)M};
+    uint64_t str[1] = {(uint64_t)(ldd * esz)};
+    uint32_t box[2] = {64, 32};
+    if (!host::encode_tmap(&td, dtype, 2, d, dims, str, box)) return GKO_ERR_INVALID;
+  }
+  GemmParams p{};
+  p.M = (int)M;
+  p.N_out = (int)N_out;
+  p.K = (int)K;
+  p.up_offset = (int)up_offset;
+  p.m_blocks = (int)((M + gemm::kBM - 1) / gemm::kBM);
+  const int bn = gemm::block_n_out(epi);
+  p.n_blocks = (int)((N_out + bn - 1) / bn);
+  p.num_tiles = p.m_blocks * p.n_blocks;
+  p.k_blocks = (int)((K + gemm::kBK - 1) / gemm::kBK);
+  p.bias = bias;
+  p.bias_kind = bias_kind;
+  p.status = status;
+  if (p.num_tiles == 0) return GKO_OK;
+  if (dtype == GKO_BF16) return dispatch_tc<__nv_bfloat16>(epi, b_mn, ta, tb, td, p, stream);
+  return dispatch_tc<__half>(epi, b_mn, ta, tb, td, p, stream);
+}
+
+int run_f32(int epi, int64_t M, int64_t N_out, int64_t K, int64_t up_offset, const float* a,
+            int64_t sam, int64_t sak, const float* b, int64_t sbk, int64_t sbn, const void* bias,
+            int bias_kind, float* d, int64_t ldd, unsigned* status, cudaStream_t stream) {
+  if (M >= (1ll << 31) || N_out >= (1ll << 31) || K >= (1ll << 31))
+    return fail(GKO_ERR_UNSUPPORTED, "GEMM dimensions must be < 2^31");
+  GemmParams p{};
+  p.M = (int)M;
+  p.N_out = (int)N_out;
+  p.K = (int)K;
+  p.up_offset = (int)up_offset;
+  p.bias = bias;
+  p.bias_kind = bias_kind;
+  p.status = status;
+  dim3 grid((unsigned)((N_out + 63) / 64), (unsigned)((M + 63) / 64));
+  if (grid.x == 0 || grid.y == 0) return GKO_OK;
+  if (grid.y > 65535) return fail(GKO_ERR_UNSUPPORTED, "fp32 GEMM supports M < 4194304");
+  switch (epi) {
+    case kEpiNone:
+      gemm_f32::kernel<kEpiNone><<<grid, 256, 0, stream>>>(a, sam, sak, b, sbk, sbn, d, ldd, p);
+      break;
+    case kEpiGelu:
+      gemm_f32::kernel<kEpiGelu><<<grid, 256, 0, stream>>>(a, sam, sak, b, sbk, sbn, d, ldd, p);
+      break;
+    case kEpiRelu:
+      gemm_f32::kernel<kEpiRelu><<<grid, 256, 0, stream>>>(a, sam, sak, b, sbk, sbn, d, ldd, p);
+      break;
+    default:
+      gemm_f32::kernel<kEpiSwiglu><<<grid, 256, 0, stream>>>(a, sam, sak, b, sbk, sbn, d, ldd, p);
+      break;
+  }
+  return host::cuda_check(cudaGetLastError(), "fp32 gemm kernel launch");
+}
+
+}  // namespace
+
+extern "C" int gko_addmm_act(int dtype, int act, int64_t m, int64_t n, int64_t k, const void* a,
+                             int64_t a_sm, int64_t a_sk, const void* b, int64_t b_sk,
+                             int64_t b_sn, const void* bias, int bias_dtype, void* d, int64_t ldd,
+                             unsigned int* status, void* stream) {
+  if (host::dtype_size(dtype) == 0) return fail(GKO_ERR_INVALID, "unknown dtype code %d", dtype);
+  if (act != GKO_ACT_NONE && act != GKO_ACT_GELU && act != GKO_ACT_RELU)
+    return fail(GKO_ERR_INVALID, "unknown activation code %d", act);
+  if (m < 0 || n < 0 || k < 0) return fail(GKO_ERR_INVALID, "negative GEMM size");
+  if ((m && n && (!d)) || (m && k && !a) || (n && k && !b))
+    return fail(GKO_ERR_INVALID, "null operand pointer");
+  const int bk = bias_kind_of(bias, bias_dtype);
+  if (bk < 0) return fail(GKO_ERR_INVALID, "unknown bias dtype code %d", bias_dtype);
+  const int epi = act == GKO_ACT_GELU ? kEpiGelu : act == GKO_ACT_RELU ? kEpiRelu : kEpiNone;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (m == 0 || n == 0) return GKO_OK;
+  if (dtype == GKO_F32)
+    return run_f32(epi, m, n, k, 0, static_cast<const float*>(a), a_sm, a_sk,
+                   static_cast<const float*>(b), b_sk, b_sn, bias, bk, static_cast<float*>(d),
+                   ldd, status, s);
+  if (k == 0) return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs k > 0");
+  if (a_sk != 1)
+    return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs a row-major mat1 (stride(-1) == 1)");
+  if (b_sk == 1) {
+    // mat2 = W^T view of a row-major weight W [n, k]: K-major B.
+    return run_tc(dtype, epi, m, n, k, n, 0, a, a_sm, b, b_sn, false, bias, bk, d, ldd, status, s);
+  }
+  if (b_sn == 1) {
+    // mat2 stored row-major [k, n]: MN-major B.
+    return run_tc(dtype, epi, m, n, k, n, 0, a, a_sm, b, b_sk, true, bias, bk, d, ldd, status, s);
+  }
+  return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs mat2 with unit stride in one dimension");
+}
+
+extern "C" int gko_linear_swiglu(int dtype, int64_t m, int64_t h, int64_t k, const void* x,
+                                 int64_t x_sm, int64_t x_sk, const void* w, int64_t w_sn,
+                                 int64_t w_sk, void* out, int64_t ldo, unsigned int* status,
+                                 void* stream) {
+  if (host::dtype_size(dtype) == 0) return fail(GKO_ERR_INVALID, "unknown dtype code %d", dtype);
+  if (m < 0 || h < 0 || k < 0) return fail(GKO_ERR_INVALID, "negative GEMM size");
+  if ((m && h && !out) || (m && k && !x) || (h && k && !w))
+    return fail(GKO_ERR_INVALID, "null operand pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (m == 0 || h == 0) return GKO_OK;
+  if (dtype == GKO_F32)
+    // logical B[k, 2h] = W^T: strides (w_sk, w_sn)
+    return run_f32(kEpiSwiglu, m, h, k, h, static_cast<const float*>(x), x_sm, x_sk,
+                   static_cast<const float*>(w), w_sk, w_sn, nullptr, kBiasNone,
+                   static_cast<float*>(out), ldo, status, s);
+  if (k == 0) return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs k > 0");
+  if (x_sk != 1)
+    return fail(GKO_ERR_UNSUPPORTED, "tensor-core SwiGLU needs a row-major x (stride(-1) == 1)");
+  if (w_sk == 1)
+    return run_tc(dtype, kEpiSwiglu, m, h, k, 2 * h, h, x, x_sm, w, w_sn, false, nullptr,
+                  kBiasNone, out, ldo, status, s);
+  if (w_sn == 1)
+    return run_tc(dtype, kEpiSwiglu, m, h, k, 2 * h, h, x, x_sm, w, w_sk, true, nullptr,
+                  kBiasNone, out, ldo, status, s);
+  return fail(GKO_ERR_UNSUPPORTED, "tensor-core SwiGLU needs a weight with unit stride in one dim");
+}

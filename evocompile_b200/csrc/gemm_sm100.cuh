@@ -1,0 +1,334 @@
+// Persistent, warp-specialised tcgen05 GEMM with fused epilogues for sm_100a.
+//
+//   D[M, N_out] = epilogue( A[M, K] * B^T )      A: K-major (row-major [M, K])
+//                                                 B: K-major ([N, K]) or MN-major ([K, N])
+//
+// Epilogues (the fused operators of the kernel catalog):
+//   kEpiNone   : D = A*B^T (+ bias)                      down-projection / plain linear
+//   kEpiGelu   : D = gelu_erf(A*B^T + bias)              gko::addmm_gelu
+//   kEpiRelu   : D = relu(A*B^T + bias)
+//   kEpiSwiglu : D = silu(A*Bg^T) * (A*Bu^T)             gko::gemm_swiglu, B = [Bg; Bu]
+//
+// CTA = 6 warps:  warp 0 TMA producer, warp 1 MMA issuer (+TMEM owner),
+//                 warps 2..5 epilogue (TMEM -> registers -> smem -> TMA store).
+// Tiles: 128 x 256 accumulator (SwiGLU: 128 gate + 128 up columns -> 128 outputs),
+// K step 64 (one 128-byte swizzle row), 4-stage smem ring, two TMEM accumulators
+// (2 x 256 columns) so the epilogue of tile i overlaps the main loop of tile i+1.
+#pragma once
+
+#include <type_traits>
+
+#include "sm100_ptx.cuh"
+
+namespace gko {
+
+enum : int { kEpiNone = 0, kEpiGelu = 1, kEpiRelu = 2, kEpiSwiglu = 3 };
+enum : int { kBiasNone = 0, kBiasF16 = 1, kBiasBF16 = 2, kBiasF32 = 3 };
+
+struct GemmParams {
+  int M;            // rows of A / D
+  int N_out;        // columns of D
+  int K;            // reduction length
+  int up_offset;    // SwiGLU: first row (K-major) / column (MN-major) of the up block in B
+  int m_blocks;     // ceil(M / 128)
+  int n_blocks;     // ceil(N_out / kBlockNOut)
+  int num_tiles;    // m_blocks * n_blocks
+  int k_blocks;     // ceil(K / 64)
+  const void* bias;
+  int bias_kind;
+  unsigned* status;
+};
+
+namespace gemm {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kMmaN = 256;
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kGroupM = 16;  // raster: 16 M-blocks share a sweep over N
+constexpr uint32_t kABytes = kBM * kBK * 2;       // 16 KB
+constexpr uint32_t kBBytes = kMmaN * kBK * 2;     // 32 KB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kStagingBytes = 4 * 2 * 32 * 128;  // 4 warps x 2 buffers x (32 rows x 128 B)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + kStagingBytes + 256;
+
+__host__ __device__ constexpr int block_n_out(int epi) { return epi == kEpiSwiglu ? 128 : 256; }
+
+__device__ __forceinline__ void tile_coords(int tile, int m_blocks, int n_blocks, int& mb, int& nb) {
+  const int group_size = kGroupM * n_blocks;
+  const int g = tile / group_size;
+  const int first_m = g * kGroupM;
+  const int gm = min(kGroupM, m_blocks - first_m);
+  const int r = tile - g * group_size;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+__device__ __forceinline__ float load_bias(const void* bias, int kind, int col, int n) {
+  if (kind == kBiasNone || col >= n) return 0.f;
+  if (kind == kBiasF32) return __ldg(reinterpret_cast<const float*>(bias) + col);
+  if (kind == kBiasBF16)
+    return __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16*>(bias) + col));
+  return __half2float(__ldg(reinterpret_cast<const __half*>(bias) + col));
+}
+
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+
+template <typename T, int EPI, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                const __grid_constant__ CUtensorMap tm_d, const GemmParams p) {
+  constexpr int kBNOut = block_n_out(EPI);
+  constexpr uint32_t kIdesc =
+      make_idesc_f16(std::is_same<T, __nv_bfloat16>::value, kBM, kMmaN, false, B_MN);
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  const uint32_t sbase = raw_addr + pad;
+  const uint32_t sA = sbase;
+  const uint32_t sB = sA + kStages * kABytes;
+  const uint32_t sStage = sB + kStages * kBBytes;
+  uint8_t* meta = smem + kStages * kStageBytes + kStagingBytes;
+  const uint32_t smeta = sStage + kStagingBytes;
+  // barriers: full[4] empty[4] tfull[2] tempty[2] drain
+  const uint32_t bar_full = smeta;
+  const uint32_t bar_empty = smeta + 8 * kStages;
+  const uint32_t bar_tfull = smeta + 16 * kStages;
+  const uint32_t bar_tempty = bar_tfull + 16;
+  const uint32_t bar_drain = bar_tempty + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 16 * kStages + 40);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 16 * kStages + 48);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar_tfull + 8 * a, 1);
+      mbar_init(bar_tempty + 8 * a, 4);
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tm_a);
+    prefetch_tmap(&tm_b);
+    prefetch_tmap(&tm_d);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag, p.status,
+                            kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full = bar_full + 8 * stage;
+          mbar_arrive_expect_tx(full, kStageBytes);
+          const uint32_t a_dst = sA + stage * kABytes;
+          const uint32_t b_dst = sB + stage * kBBytes;
+          const int k0 = kb * kBK;
+          tma_load_2d(a_dst, &tm_a, full, k0, mb * kBM);
+          if constexpr (!B_MN) {
+            // B is [N, K] K-major: two 128-row boxes.
+            if constexpr (EPI == kEpiSwiglu) {
+              tma_load_2d(b_dst, &tm_b, full, k0, nb * 128);
+              tma_load_2d(b_dst + kBBytes / 2, &tm_b, full, k0, p.up_offset + nb * 128);
+            } else {
+              tma_load_2d(b_dst, &tm_b, full, k0, nb * 256);
+              tma_load_2d(b_dst + kBBytes / 2, &tm_b, full, k0, nb * 256 + 128);
+            }
+          } else {
+            // B is [K, N] MN-major: four 64-column boxes, 64 K-rows each.
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              int col;
+              if constexpr (EPI == kEpiSwiglu)
+                col = (c < 2) ? nb * 128 + c * 64 : p.up_offset + nb * 128 + (c - 2) * 64;
+              else
+                col = nb * 256 + c * 64;
+              tma_load_2d(b_dst + c * (kBBytes / 4), &tm_b, full, col, k0);
+            }
+          }
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!wait_bounded(bar_tempty + 8 * acc, acc_phase ^ 1, abort_flag, p.status,
+                          kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kMmaN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bounded(bar_full + 8 * stage, phase, abort_flag, p.status,
+                            kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = sA + stage * kABytes;
+          const uint32_t b_addr = sB + stage * kBBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t adesc = make_sdesc_sw128(a_addr + kk * 32, 16, 1024);
+            uint64_t bdesc;
+            if constexpr (!B_MN)
+              bdesc = make_sdesc_sw128(b_addr + kk * 32, 16, 1024);
+            else
+              bdesc = make_sdesc_sw128(b_addr + kk * 16 * 128, kBBytes / 4, 1024);
+            mma_f16_ss(d_tmem, adesc, bdesc, kIdesc, (kb | kk) != 0);
+          }
+          mma_commit(bar_empty + 8 * stage);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(bar_tfull + 8 * acc);
+      }
+      if (*abort_flag) {
+        // Drain this thread's tensor-core work before the TMEM is released.
+        mma_commit(bar_drain);
+        wait_for(bar_drain, 0, p.status, kStatusTimeoutDrain);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int ew = warp - 2;
+    const uint32_t stg0 = sStage + ew * (2 * 32 * 128);
+    int local = 0;
+    int issued = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
+      int mb, nb;
+      tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!wait_bounded(bar_tfull + 8 * acc, acc_phase, abort_flag, p.status,
+                        kStatusTimeoutEpilogue))
+        break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + acc * kMmaN + (static_cast<uint32_t>(quarter * 32) << 16);
+      const int row0 = mb * kBM + quarter * 32;
+      const int col_base = nb * kBNOut;
+#pragma unroll 1
+      for (int c = 0; c < kBNOut / 64; ++c) {
+        const uint32_t buf = stg0 + (issued & 1) * (32 * 128);
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int col0 = c * 64 + h * 32;
+          uint32_t packed[16];
+          if constexpr (EPI == kEpiSwiglu) {
+            uint32_t g[32], u[32];
+            tmem_ld32(t_row + col0, g);
+            tmem_ld32(t_row + 128 + col0, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
+              const float u0 = __uint_as_float(u[2 * i]), u1 = __uint_as_float(u[2 * i + 1]);
+              packed[i] = Cvt<T>::pack(silu(g0) * u0, silu(g1) * u1);
+            }
+          } else {
+            uint32_t v[32];
+            tmem_ld32(t_row + col0, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float x0 = __uint_as_float(v[2 * i]);
+              float x1 = __uint_as_float(v[2 * i + 1]);
+              if (p.bias_kind != kBiasNone) {
+                x0 += load_bias(p.bias, p.bias_kind, col_base + col0 + 2 * i, p.N_out);
+                x1 += load_bias(p.bias, p.bias_kind, col_base + col0 + 2 * i + 1, p.N_out);
+              }
+              if constexpr (EPI == kEpiGelu) {
+                x0 = gelu_erf(x0);
+                x1 = gelu_erf(x1);
+              } else if constexpr (EPI == kEpiRelu) {
+                x0 = fmaxf(x0, 0.f);
+                x1 = fmaxf(x1, 0.f);
+              }
+              packed[i] = Cvt<T>::pack(x0, x1);
+            }
+          }
+          // 128B-swizzled staging row: 16-byte piece j of row `lane` lives at j ^ (lane & 7).
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int piece = h * 4 + j;
+            const uint32_t addr = buf + lane * 128 + ((piece ^ (lane & 7)) << 4);
+            st_shared_v4(addr, packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
+                         packed[4 * j + 3]);
+          }
+        }
+        if (c == kBNOut / 64 - 1) {
+          // All TMEM reads of this accumulator are done: hand it back to the MMA warp.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tm_d, buf, col_base + c * 64, row0);
+          bulk_commit_group();
+        }
+        ++issued;
+      }
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+}  // namespace gemm
+}  // namespace gko

@@ -1,0 +1,284 @@
+"""Tensor-level host code for the fused operators: validates torch tensors,
+allocates outputs, and calls the C ABI of libgko_b200.so on the current stream.
+
+These functions are what the ``gko::`` custom ops (``evocompile_b200.kernels``)
+run. Each raises RuntimeError for inputs the kernels do not implement; none of
+them falls back to another implementation.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_I64x4 = ctypes.c_int64 * 4
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _status_ptr(dev):
+    return ctypes.c_void_p(_lib.status_word(dev).data_ptr())
+
+
+def _stream(dev):
+    return ctypes.c_void_p(_lib.stream_ptr(dev))
+
+
+# --------------------------------------------------------------------------- GEMM
+def addmm_act(bias, mat1, mat2, act: int = _lib.ACT_GELU):
+    """act(mat1 @ mat2 + bias) with mat1 [..., K] and mat2 [K, N].
+
+    Follows the contract of gko::addmm_gelu (eval/kernels/addmm_gelu.py:150-161,
+    192-210): output shape mat1.shape[:-1] + (N,), dtype of mat1. mat2 is
+    usually the transposed view W^T of a Linear weight and is read in place.
+    """
+    dev = _lib.require_cuda(mat1, mat2, bias)
+    if mat2.dim() != 2:
+        raise RuntimeError(f"addmm_gelu: mat2 must be 2-D, got shape {tuple(mat2.shape)}")
+    if mat1.dim() < 1:
+        raise RuntimeError("addmm_gelu: mat1 must have at least one dimension")
+    if mat1.dtype != mat2.dtype:
+        raise RuntimeError(f"addmm_gelu: mat1 {mat1.dtype} and mat2 {mat2.dtype} differ")
+    K = mat1.shape[-1]
+    if mat2.shape[0] != K:
+        raise RuntimeError(f"addmm_gelu: K mismatch {K} vs {mat2.shape[0]}")
+    N = mat2.shape[1]
+    dt = _lib.dtype_code(mat1.dtype)
+    lead = mat1.shape[:-1]
+    a = mat1.reshape(-1, K) if mat1.dim() != 2 else mat1
+    M = a.shape[0]
+    if dt != _lib.F32 and a.stride(-1) != 1 and M > 1:
+        a = a.contiguous()
+    b = mat2
+    if dt != _lib.F32 and not (b.stride(0) == 1 or b.stride(1) == 1):
+        b = b.contiguous()
+    bias_t = None
+    bias_dt = 0
+    if bias is not None and bias.numel() > 0:
+        if bias.numel() == N:
+            bias_t = bias.reshape(N)
+        elif bias.numel() == 1:
+            bias_t = bias.reshape(1).expand(N)
+        else:
+            raise RuntimeError(
+                f"addmm_gelu: bias must broadcast along rows (numel N={N}); got shape {tuple(bias.shape)}"
+            )
+        if bias_t.stride(0) != 1:
+            bias_t = bias_t.contiguous()
+        bias_dt = _lib.dtype_code(bias_t.dtype)
+    out = torch.empty((M, N), device=dev, dtype=mat1.dtype)
+    if M and N:
+        with torch.cuda.device(dev):
+            a_sm = a.stride(0) if M > 1 else max(K, 8)
+            rc = _lib.load().gko_addmm_act(
+                dt, act, M, N, K, _ptr(a), a_sm, a.stride(1), _ptr(b), b.stride(0), b.stride(1),
+                _ptr(bias_t), bias_dt, _ptr(out), out.stride(0), _status_ptr(dev), _stream(dev),
+            )
+        _lib.check(rc, "gko_addmm_act")
+    return out.reshape(*lead, N)
+
+
+def linear(x, weight, bias=None):
+    """x @ weight.T (+ bias) on the tensor-core GEMM (the down-projection path)."""
+    return addmm_act(bias, x, weight.t(), _lib.ACT_NONE)
+
+
+def linear_swiglu(x, weight):
+    """silu(x @ Wg.T) * (x @ Wu.T) with weight = [Wg; Wu] of shape (2H, D).
+
+    Contract of gko::gemm_swiglu (eval/kernels/gemm_swiglu.py:147-169,
+    208-220): x (..., D) -> (..., H), dtype of x.
+    """
+    dev = _lib.require_cuda(x, weight)
+    if weight.dim() != 2 or weight.shape[0] % 2:
+        raise RuntimeError(f"gemm_swiglu: weight must be (2H, D), got {tuple(weight.shape)}")
+    if x.dtype != weight.dtype:
+        raise RuntimeError(f"gemm_swiglu: x {x.dtype} and weight {weight.dtype} differ")
+    D = x.shape[-1]
+    if weight.shape[1] != D:
+        raise RuntimeError(f"gemm_swiglu: shape mismatch x={tuple(x.shape)} weight={tuple(weight.shape)}")
+    H = weight.shape[0] // 2
+    dt = _lib.dtype_code(x.dtype)
+    lead = x.shape[:-1]
+    a = x.reshape(-1, D)
+    M = a.shape[0]
+    if dt != _lib.F32 and a.stride(-1) != 1 and M > 1:
+        a = a.contiguous()
+    w = weight
+    if dt != _lib.F32 and not (w.stride(0) == 1 or w.stride(1) == 1):
+        w = w.contiguous()
+    out = torch.empty((M, H), device=dev, dtype=x.dtype)
+    if M and H:
+        with torch.cuda.device(dev):
+            a_sm = a.stride(0) if M > 1 else max(D, 8)
+            rc = _lib.load().gko_linear_swiglu(
+                dt, M, H, D, _ptr(a), a_sm, a.stride(1), _ptr(w), w.stride(0), w.stride(1),
+                _ptr(out), out.stride(0), _status_ptr(dev), _stream(dev),
+            )
+        _lib.check(rc, "gko_linear_swiglu")
+    return out.reshape(*lead, H)
+
+
+def swiglu_mlp(x, w_gate_up, w_down):
+    """(silu(x Wg^T) * (x Wu^T)) Wdown^T: the fused gate/up kernel then the down GEMM."""
+    return linear(linear_swiglu(x, w_gate_up), w_down)
+
+
+def silu_mul(x, y):
+    """silu(x) * y elementwise (gko::silu_mul, eval/kernels/silu_mul.py:29-43)."""
+    dev = _lib.require_cuda(x, y)
+    if x.shape != y.shape or x.dtype != y.dtype:
+        raise RuntimeError(f"silu_mul: operands differ: {tuple(x.shape)} {x.dtype} vs {tuple(y.shape)} {y.dtype}")
+    xc = x.contiguous()
+    yc = y.contiguous()
+    out = torch.empty_like(xc)
+    n = xc.numel()
+    if n:
+        with torch.cuda.device(dev):
+            rc = _lib.load().gko_silu_mul(
+                _lib.dtype_code(x.dtype), n, _ptr(xc), _ptr(yc), _ptr(out), _status_ptr(dev), _stream(dev)
+            )
+        _lib.check(rc, "gko_silu_mul")
+    return out
+
+
+# --------------------------------------------------------------------------- attention
+def _bias_layout(q, k, attn_bias):
+    """Map an additive attention bias onto the kernel's bias modes.
+
+    Accepts the layouts of the reference's _bias_pack
+    (eval/kernels/fused_sdpa.py:546-575): 1-D/2-D/3-D key padding holding
+    z * n_k values, [z|1, 1, 1, n_k] rows, and [z|1|nW, h|1, n_q, n_k] full
+    biases with broadcast dims read through stride 0 (no [z, h, n_q, n_k]
+    materialisation). Returns (tensor, mode, strides[4], batches).
+    """
+    z, h, n_q, _ = q.shape
+    n_k = k.shape[-2]
+    if attn_bias is None or attn_bias.numel() == 0:
+        return None, _lib.BIAS_NONE, (0, 0, 0, 0), 1
+    b = attn_bias
+    if b.dim() <= 2 and b.numel() == z * n_k:
+        b = b.reshape(z, n_k)
+        return b, _lib.BIAS_KEYPAD, (b.stride(0), 0, 0, b.stride(1)), z
+    if b.dim() == 3 and b.shape[-1] == n_k and b.numel() == z * n_k:
+        b = b.reshape(z, n_k)
+        return b, _lib.BIAS_KEYPAD, (b.stride(0), 0, 0, b.stride(1)), z
+    if b.dim() == 4 and b.shape[-2] == 1 and b.shape[-1] == n_k:
+        if b.shape[0] == z:
+            row = b[:, 0, 0, :]
+            return row, _lib.BIAS_KEYPAD, (row.stride(0), 0, 0, row.stride(1)), z
+        if b.shape[0] == 1:
+            row = b[0, 0, 0, :]
+            return row, _lib.BIAS_KEYPAD, (0, 0, 0, row.stride(0)), z
+    if b.dim() == 4 and b.shape[-2] == n_q and b.shape[-1] == n_k:
+        bz, bh = b.shape[0], b.shape[1]
+        if bh not in (1, h):
+            raise RuntimeError(f"attention bias head dim {bh} must be 1 or {h}")
+        if bz == z:
+            nb = z
+        elif bz == 1:
+            nb = z
+        elif z % bz == 0:
+            nb = bz  # shifted-window mask [nW, h, n, n] against q [B * nW, h, n, d]
+        else:
+            raise RuntimeError(f"attention bias batch {bz} does not divide the batch {z}")
+        sz = b.stride(0) if bz > 1 else 0
+        sh = b.stride(1) if bh > 1 else 0
+        sq = b.stride(2) if n_q > 1 else 0
+        return b, _lib.BIAS_FULL, (sz, sh, sq, b.stride(3)), nb
+    raise RuntimeError(
+        f"unsupported attention bias shape {tuple(attn_bias.shape)} for q {tuple(q.shape)}, k {tuple(k.shape)}"
+    )
+
+
+def fmha_fwd(q, k, v, attn_bias=None, scale=None, causal=0, window=0, softcap=0.0):
+    """Fused attention forward -> (out [z, hq, sq, d] contiguous, lse f32 [z * hq, sq]).
+
+    q [z, hq, sq, d], k/v [z, hkv, sk, d] with hq % hkv == 0 (GQA); any
+    strides with unit stride along d (e.g. [z, s, h, d] storage viewed through
+    transpose(1, 2)) are read in place. Contract of gko::fused_sdpa_pair
+    (eval/kernels/fused_sdpa.py:912-943).
+    """
+    dev = _lib.require_cuda(q, k, v, attn_bias)
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise RuntimeError("fmha: q, k, v must be 4-D [z, h, s, d]")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise RuntimeError("fmha: q, k, v dtypes differ")
+    z, hq, sq, d = q.shape
+    _, hkv, sk, dk = k.shape
+    if k.shape != v.shape or dk != d or k.shape[0] != z:
+        raise RuntimeError(f"fmha: shape mismatch q={tuple(q.shape)} k={tuple(k.shape)} v={tuple(v.shape)}")
+    if scale is None:
+        scale = d ** -0.5
+    dt = _lib.dtype_code(q.dtype)
+
+    def _fix(t):
+        if t.stride(-1) != 1 or any(s % 8 for s in t.stride()[:3]) or t.data_ptr() % 16:
+            return t.contiguous()
+        return t
+
+    q, k, v = _fix(q), _fix(k), _fix(v)
+    bias_t, mode, bstr, nb = _bias_layout(q, k, attn_bias)
+    out = torch.empty((z, hq, sq, d), device=dev, dtype=q.dtype)
+    lse = torch.empty((z * hq, sq), device=dev, dtype=torch.float32)
+    if z and hq and sq:
+        with torch.cuda.device(dev):
+            rc = _lib.load().gko_fmha_fwd(
+                dt, z, hq, hkv, sq, sk, d,
+                _ptr(q), _I64x4(*q.stride()), _ptr(k), _I64x4(*k.stride()), _ptr(v), _I64x4(*v.stride()),
+                _ptr(bias_t), mode, _lib.dtype_code(bias_t.dtype) if bias_t is not None else 0,
+                _I64x4(*bstr), nb, float(scale), int(bool(causal)), int(window or 0), float(softcap or 0.0),
+                _ptr(out), _ptr(lse), _status_ptr(dev), _stream(dev),
+            )
+        _lib.check(rc, "gko_fmha_fwd")
+    return out, lse
+
+
+def fmha_varlen_fwd(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k=None, scale=None,
+                    causal=0, window=0, softcap=0.0):
+    """Attention over packed sequences -> (out [tq, hq, d], lse f32 [hq, tq]).
+
+    q [tq, hq, d], k/v [tk, hkv, d]; cu_seqlens_* int32 [b + 1] on the device.
+    """
+    dev = _lib.require_cuda(q, k, v, cu_seqlens_q, cu_seqlens_k)
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
+        raise RuntimeError("fmha_varlen: q, k, v must be 3-D [tokens, heads, d]")
+    if q.dtype != k.dtype or q.dtype != v.dtype:
+        raise RuntimeError("fmha_varlen: q, k, v dtypes differ")
+    if cu_seqlens_q.dtype != torch.int32 or cu_seqlens_k.dtype != torch.int32:
+        raise RuntimeError("fmha_varlen: cu_seqlens must be int32")
+    if cu_seqlens_q.numel() != cu_seqlens_k.numel() or cu_seqlens_q.numel() < 1:
+        raise RuntimeError("fmha_varlen: cu_seqlens_q and cu_seqlens_k must both have b + 1 entries")
+    tq, hq, d = q.shape
+    tk, hkv, dk = k.shape
+    if k.shape != v.shape or dk != d:
+        raise RuntimeError(f"fmha_varlen: shape mismatch q={tuple(q.shape)} k={tuple(k.shape)}")
+    if scale is None:
+        scale = d ** -0.5
+    b = cu_seqlens_q.numel() - 1
+
+    def _fix(t):
+        if t.stride(-1) != 1 or t.stride(0) % 8 or t.stride(1) % 8 or t.data_ptr() % 16:
+            return t.contiguous()
+        return t
+
+    q, k, v = _fix(q), _fix(k), _fix(v)
+    cq = cu_seqlens_q.contiguous()
+    ck = cu_seqlens_k.contiguous()
+    out = torch.empty((tq, hq, d), device=dev, dtype=q.dtype)
+    lse = torch.empty((hq, tq), device=dev, dtype=torch.float32)
+    if b and tq and hq:
+        with torch.cuda.device(dev):
+            rc = _lib.load().gko_fmha_varlen_fwd(
+                _lib.dtype_code(q.dtype), b, hq, hkv, d, tq, tk, int(max_seqlen_q),
+                _ptr(q), q.stride(0), q.stride(1), _ptr(k), k.stride(0), k.stride(1), _ptr(v), v.stride(0),
+                v.stride(1), _ptr(cq), _ptr(ck), float(scale), int(bool(causal)), int(window or 0),
+                float(softcap or 0.0), _ptr(out), _ptr(lse), _status_ptr(dev), _stream(dev),
+            )
+        _lib.check(rc, "gko_fmha_varlen_fwd")
+    return out, lse

@@ -1,0 +1,162 @@
+/*
+ * gko_b200.h — C ABI of the B200 (sm_100a) fused-operator library.
+ *
+ * One shared library, libgko_b200.so, exports the entry points below. They take
+ * plain device pointers, sizes and element strides (never framework types),
+ * launch on the given CUDA stream (NULL = legacy default stream) and return
+ * GKO_OK or an error code; gko_last_error() then holds a message naming the
+ * violated constraint. Nothing here falls back to another implementation: an
+ * input the kernels do not support is rejected.
+ *
+ * Every kernel bounds each of its internal waits. If one expires, the kernel
+ * ORs a GKO_STATUS_* bit into *status (a caller-owned device word; may be NULL),
+ * drains its own tensor-core work, frees its tensor memory and returns, so the
+ * CUDA context stays usable. The host reads the word after synchronising.
+ *
+ * Each declaration names the reference interface it replaces
+ * (paths relative to the EvoCompile repository).
+ */
+#ifndef GKO_B200_H
+#define GKO_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define GKO_F16 1
+#define GKO_BF16 2
+#define GKO_F32 3
+
+/* GEMM epilogue activations */
+#define GKO_ACT_NONE 0
+#define GKO_ACT_GELU 1 /* exact erf GELU: 0.5 x (1 + erf(x / sqrt 2)) */
+#define GKO_ACT_RELU 2
+
+/* attention bias layouts */
+#define GKO_BIAS_NONE 0
+#define GKO_BIAS_KEYPAD 1 /* additive [z, sk] row per batch (key padding) */
+#define GKO_BIAS_FULL 2   /* additive [z, h, sq, sk] with broadcast (stride 0) allowed */
+
+/* return codes */
+#define GKO_OK 0
+#define GKO_ERR_INVALID 1     /* bad sizes, strides, pointers */
+#define GKO_ERR_UNSUPPORTED 2 /* valid input outside what the kernels implement */
+#define GKO_ERR_CUDA 3        /* CUDA runtime / driver error */
+
+/* status-word bits written by kernels */
+#define GKO_STATUS_TIMEOUT_PRODUCER 0x1u
+#define GKO_STATUS_TIMEOUT_MMA 0x2u
+#define GKO_STATUS_TIMEOUT_EPILOGUE 0x4u
+#define GKO_STATUS_TIMEOUT_SOFTMAX 0x8u
+#define GKO_STATUS_TIMEOUT_DRAIN 0x10u
+
+/* Message for the last error returned on this host thread ("" if none). */
+const char* gko_last_error(void);
+
+/* Library ABI version (major * 100 + minor). */
+int gko_version(void);
+
+/*
+ * D[m, n] = act(sum_k A[m, k] * B[k, n] + bias[n])
+ *
+ * Replaces ext.addmm_epilogue(bias, mat1, mat2, act)
+ * (eval/kernels/cutlass_fmha/gko_cutlass_attn.cu:552-586, binding :588-591) and the
+ * Triton launch _triton_addmm_gelu (eval/kernels/addmm_gelu.py:87-118) behind
+ * gko::addmm_gelu (eval/kernels/addmm_gelu.py:192-223).
+ *
+ * A (mat1) is [m, k] with element strides (a_sm, a_sk); B (mat2) is the
+ * logical [k, n] operand with strides (b_sk, b_sn) — a transposed weight view
+ * (b_sk == 1) is read in place. bias is NULL or a length-n vector of
+ * bias_dtype. D is [m, n] with row stride ldd, same dtype as A.
+ * f16/bf16 run on tcgen05 tensor cores (f32 accumulate) and need
+ * a_sk == 1 and (b_sk == 1 or b_sn == 1), 16-byte aligned bases and row
+ * strides that are multiples of 8 elements. f32 runs exact fp32 FMA on any strides.
+ */
+int gko_addmm_act(int dtype, int act, int64_t m, int64_t n, int64_t k, const void* a, int64_t a_sm,
+                  int64_t a_sk, const void* b, int64_t b_sk, int64_t b_sn, const void* bias,
+                  int bias_dtype, void* d, int64_t ldd, unsigned int* status, void* stream);
+
+/*
+ * out[m, h] = silu(sum_k x[m, k] Wg[h, k]) * (sum_k x[m, k] Wu[h, k]),  W = [Wg; Wu] is [2h, k]
+ *
+ * Replaces ext.linear_swiglu(x, weight)
+ * (eval/kernels/cutlass_fmha/gko_cutlass_swiglu.cu:287-326, binding :330-335) and the
+ * Triton launch _triton_gemm_swiglu (eval/kernels/gemm_swiglu.py:112-144) behind
+ * gko::gemm_swiglu (eval/kernels/gemm_swiglu.py:147-169,208-232). One kernel: the
+ * [m, 2h] gate/up intermediate never reaches memory.
+ *
+ * x is [m, k] with strides (x_sm, x_sk); W is [2h, k] with strides (w_sn, w_sk)
+ * (w_sk == 1 is the F.linear layout; w_sn == 1 is read as a transposed view).
+ * out is [m, h] with row stride ldo, same dtype as x.
+ */
+int gko_linear_swiglu(int dtype, int64_t m, int64_t h, int64_t k, const void* x, int64_t x_sm,
+                      int64_t x_sk, const void* w, int64_t w_sn, int64_t w_sk, void* out,
+                      int64_t ldo, unsigned int* status, void* stream);
+
+/*
+ * Fused multi-head attention forward (dense batch).
+ *   out = softmax(mask(softcap(scale * Q K^T + bias))) V,  lse = m + ln(l) per row
+ *
+ * Replaces ext.fmha_fwd(q, k, v, bias, scale, causal, window, softcap)
+ * (eval/kernels/cutlass_fmha/gko_cutlass_attn.cu:371-461, binding :588) and the
+ * Triton launch _triton_fwd (eval/kernels/fused_sdpa.py:614-665) behind
+ * gko::fused_sdpa_pair / gko::cutlass_fmha_pair (eval/kernels/fused_sdpa.py:912-943,
+ * eval/kernels/cutlass_gemm_attn.py:81-121).
+ *
+ * q is logical [z, hq, sq, d], k and v are [z, hkv, sk, d] (hq % hkv == 0:
+ * grouped-query heads h use kv head h / (hq / hkv)). *_strides give element
+ * strides for (z, h, s, d); the d stride must be 1, the others multiples of 8,
+ * so [z, s, h, d] storage viewed as [z, h, s, d] is read in place.
+ * bias: GKO_BIAS_NONE, GKO_BIAS_KEYPAD (bias_strides[0] = z stride,
+ * bias_strides[3] = key stride) or GKO_BIAS_FULL (strides for z, h, q, key;
+ * 0 broadcasts). The bias holds bias_batch batches (dividing z); batch b of
+ * q reads bias batch b % bias_batch (a shifted-window mask [nW, h, sq, sk]). causal keeps key <= query (top-left aligned); window > 0 keeps
+ * |key - query| <= window; softcap > 0 applies softcap * tanh(x / softcap)
+ * (x clamped to +-15 softcap first). Masked scores never contribute; a row
+ * with every key masked yields zeros and lse = -inf.
+ * out is contiguous [z, hq, sq, d] (same dtype as q), lse is f32 [z * hq, sq].
+ * dtype: GKO_F16 or GKO_BF16; d in {64, 128}.
+ */
+int gko_fmha_fwd(int dtype, int64_t z, int64_t hq, int64_t hkv, int64_t sq, int64_t sk, int64_t d,
+                 const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                 const void* v, const int64_t* v_strides, const void* bias, int bias_mode,
+                 int bias_dtype, const int64_t* bias_strides, int64_t bias_batch, float scale,
+                 int causal, int window, float softcap, void* out, float* lse,
+                 unsigned int* status, void* stream);
+
+/*
+ * Fused multi-head attention forward over packed variable-length sequences.
+ *
+ * New entry point (no reference counterpart: the reference's attention takes
+ * only dense [z, h, s, d] batches, eval/kernels/fused_sdpa.py:535-543); it
+ * backs gko::fmha_varlen_fwd. Sequence i owns query rows
+ * [cu_seqlens_q[i], cu_seqlens_q[i+1]) and key rows [cu_seqlens_k[i], cu_seqlens_k[i+1]).
+ * q is [tq, hq, d], k and v are [tk, hkv, d], with element strides (token, head)
+ * (d stride 1). cu_seqlens_* are device int32 arrays of b + 1 entries;
+ * max_seqlen_q bounds every query length. out is contiguous [tq, hq, d],
+ * lse is f32 [hq, tq]. Masks and GQA as for gko_fmha_fwd (no bias).
+ */
+int gko_fmha_varlen_fwd(int dtype, int64_t b, int64_t hq, int64_t hkv, int64_t d, int64_t tq,
+                        int64_t tk, int64_t max_seqlen_q, const void* q, int64_t q_st,
+                        int64_t q_sh, const void* k, int64_t k_st, int64_t k_sh, const void* v,
+                        int64_t v_st, int64_t v_sh, const int32_t* cu_seqlens_q,
+                        const int32_t* cu_seqlens_k, float scale, int causal, int window,
+                        float softcap, void* out, float* lse, unsigned int* status, void* stream);
+
+/*
+ * out[i] = silu(x[i]) * y[i] over n contiguous elements (dtype f16, bf16 or f32).
+ *
+ * Replaces the Triton launch _triton (eval/kernels/silu_mul.py:33-43) behind
+ * gko::silu_mul (eval/kernels/silu_mul.py:66-88). Buffers 16-byte aligned.
+ */
+int gko_silu_mul(int dtype, int64_t n, const void* x, const void* y, void* out,
+                 unsigned int* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GKO_B200_H */
