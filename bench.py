@@ -1,0 +1,583 @@
+"""Benchmark of the fused operators on B200 — prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+Default workload (the headline): the SwiGLU MLP at the Llama-3-8B shape, bf16,
+per GPU X[8192, 4096], W_gate/W_up [14336, 4096] (packed [W_gate; W_up]),
+W_down [4096, 14336]; one step = gko::gemm_swiglu (one fused tcgen05 kernel)
+followed by the down-projection GEMM (one tcgen05 kernel). Multi-GPU runs are
+token-sharded with replicated weights (weak scaling: 8192 tokens per GPU, no
+data-path collective); N > 1 is launched by torchrun, one rank per GPU.
+
+Other workloads (for measurement; the default line uses swiglu):
+  addmm_gelu   X[8192, 4096] @ W[14336, 4096]^T + b, exact GELU
+  fmha_causal  causal attention B=8 H=32 S=4096 D=128 in [B, S, H, D] (heads sharded at N > 1)
+  fmha_varlen  GQA varlen causal, Hq=64 Hkv=8 D=128, 16 sequences L ~ U[512, 8192] (seed 0)
+
+Timing: W untimed warm-up steps, then K steps between a barrier +
+synchronize on both sides, timed with CUDA events on the launching stream;
+the max over ranks is reported. Inputs are larger than the 126 MB L2 (no
+flush needed). ``e2e`` repeats the step through the public operator API with
+the activations copied in from pinned host memory and the result copied back
+inside the timed region. ``--impl reference`` times the CPU restatement of the
+reference's eager path on the host cores (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
+TRAFFIC_FILE = REPO / "profiles" / "traffic.txt"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC = "fused-kernel TFLOP/s"
+
+
+# --------------------------------------------------------------------------- helpers
+def peaks():
+    try:
+        p = json.loads(PEAKS_FILE.read_text())
+        return p, "measured"
+    except Exception:
+        return FALLBACK_PEAKS, "fallback"
+
+
+def traffic_per_launch(kernel_key: str):
+    """DRAM bytes (read + write) per launch of a kernel, from the committed ncu summary."""
+    try:
+        for line in TRAFFIC_FILE.read_text().splitlines():
+            parts = line.split()
+            if parts and parts[0] == kernel_key:
+                for p in parts[1:]:
+                    if p.startswith("dram_bytes_per_launch="):
+                        return float(p.split("=", 1)[1])
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.out = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            sel = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:
+            sel = str(device_index)
+        self.cmd = ["nvidia-smi", "-i", sel, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                    "-lms", "100"]
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self):
+        if not self.out:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.out.strip().splitlines():
+            cols = [c.strip() for c in line.split(",")]
+            if len(cols) < 7:
+                continue
+            try:
+                sm.append(float(cols[0]))
+                smax.append(float(cols[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, cols[3:7]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        busy = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    from evocompile_b200.shard import max_over_ranks as m
+
+    return m(v)
+
+
+# --------------------------------------------------------------------------- workloads
+class SwigluMLP:
+    name = "swiglu"
+    dominant = "swiglu_gateup"
+
+    def __init__(self, dev, world, rank):
+        from evocompile_b200 import ops
+
+        self.ops = ops
+        self.T, self.D, self.H = 8192, 4096, 14336
+        g = torch.Generator(device=dev).manual_seed(1000 + rank)
+        self.x = torch.randn(self.T, self.D, device=dev, generator=g).to(torch.bfloat16)
+        self.wgu = (torch.randn(2 * self.H, self.D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        self.wd = (torch.randn(self.D, self.H, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        self.flop_gateup = 2.0 * self.T * self.D * 2 * self.H
+        self.flop_step = self.flop_gateup + 2.0 * self.T * self.H * self.D
+        self.launches_per_step = 2
+        self.config = {
+            "workload": "swiglu_mlp llama3-8b shape: X[8192,4096] bf16, W_gate/W_up[14336,4096] packed [28672,4096], "
+                        "W_down[4096,14336]; step = fused gate/up+SwiGLU kernel + down-proj GEMM",
+            "model": "Llama-3-8B MLP (synthetic random-init weights N(0,0.02), X ~ N(0,1))",
+            "tokens_per_gpu": self.T, "global_batch": self.T * world, "seq_len": None,
+            "parallelism": f"dp{world} (token-sharded, weights replicated)",
+            "l2": "operands 0.64 GB per GPU > 126 MB L2; no flush",
+        }
+
+    def step(self, ev=None):
+        if ev is not None:
+            ev[0].record()
+        h = self.ops.linear_swiglu(self.x, self.wgu)
+        if ev is not None:
+            ev[1].record()
+        return self.ops.linear(h, self.wd)
+
+    # public-API end to end: pinned host activations in, result out
+    def e2e_setup(self):
+        from evocompile_b200.kernels import gemm_swiglu
+
+        self.api = gemm_swiglu
+        self.x_host = self.x.cpu().pin_memory()
+        self.out_host = torch.empty(self.T, self.D, dtype=torch.bfloat16).pin_memory()
+        self.x_dev = torch.empty_like(self.x)
+        return self.x_host.numel() * 2, self.out_host.numel() * 2
+
+    def e2e_step(self):
+        self.x_dev.copy_(self.x_host, non_blocking=True)
+        out = self.api.swiglu_mlp(self.x_dev, self.wgu, self.wd)
+        self.out_host.copy_(out, non_blocking=True)
+
+    def torch_reference(self):
+        import torch.nn.functional as F
+
+        def mlp(x, wgu, wd):
+            g, u = F.linear(x, wgu).chunk(2, dim=-1)
+            return F.linear(F.silu(g) * u, wd)
+
+        return mlp, (self.x, self.wgu, self.wd)
+
+    def cpu_sample(self):
+        """512-token sample of the same MLP for the CPU restatement (fp32)."""
+        import oracle
+
+        xs = self.x[:512].float().cpu()
+        wgu, wd = self.wgu.float().cpu(), self.wd.float().cpu()
+        flops = 2.0 * 512 * self.D * 2 * self.H + 2.0 * 512 * self.H * self.D
+        return (lambda: oracle.swiglu_mlp(xs, wgu, wd)), flops, \
+            "512 of the 8192 tokens through the full MLP (fp32 oracle restating _eager_gemm_swiglu + F.linear)"
+
+
+class AddmmGelu(SwigluMLP):
+    name = "addmm_gelu"
+    dominant = "addmm_gelu"
+
+    def __init__(self, dev, world, rank):
+        from evocompile_b200 import ops
+
+        self.ops = ops
+        self.T, self.D, self.N = 8192, 4096, 14336
+        g = torch.Generator(device=dev).manual_seed(2000 + rank)
+        self.x = torch.randn(self.T, self.D, device=dev, generator=g).to(torch.bfloat16)
+        self.w = (torch.randn(self.N, self.D, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        self.b = (torch.randn(self.N, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+        self.flop_gateup = self.flop_step = 2.0 * self.T * self.D * self.N
+        self.launches_per_step = 1
+        self.config = {"workload": "addmm_gelu bf16: X[8192,4096] W[14336,4096] b[14336], exact GELU",
+                       "tokens_per_gpu": self.T, "global_batch": self.T * world,
+                       "parallelism": f"dp{world} (token-sharded)", "l2": "operands > L2; no flush"}
+
+    def step(self, ev=None):
+        if ev is not None:
+            ev[0].record()
+        out = self.ops.addmm_act(self.b, self.x, self.w.t())
+        if ev is not None:
+            ev[1].record()
+        return out
+
+    def e2e_setup(self):
+        from evocompile_b200.kernels import addmm_gelu
+
+        addmm_gelu.register()
+        self.x_host = self.x.cpu().pin_memory()
+        self.out_host = torch.empty(self.T, self.N, dtype=torch.bfloat16).pin_memory()
+        self.x_dev = torch.empty_like(self.x)
+        return self.x_host.numel() * 2, self.out_host.numel() * 2
+
+    def e2e_step(self):
+        self.x_dev.copy_(self.x_host, non_blocking=True)
+        out = torch.ops.gko.addmm_gelu(self.b, self.x_dev, self.w.t())
+        self.out_host.copy_(out, non_blocking=True)
+
+    def torch_reference(self):
+        import torch.nn.functional as F
+
+        return (lambda x, w, b: F.gelu(F.linear(x, w, b))), (self.x, self.w, self.b)
+
+    def cpu_sample(self):
+        import oracle
+
+        xs, w, b = self.x[:512].float().cpu(), self.w.float().cpu(), self.b.float().cpu()
+        return (lambda: oracle.addmm_gelu(b, xs, w.t())), 2.0 * 512 * self.D * self.N, "512 of 8192 rows (fp32 oracle)"
+
+
+class FmhaCausal(SwigluMLP):
+    name = "fmha_causal"
+    dominant = "fmha_fwd"
+
+    def __init__(self, dev, world, rank):
+        from evocompile_b200 import ops
+
+        self.ops = ops
+        B, S, H, D = 8, 4096, 32, 128
+        h = H // world  # heads sharded
+        self.B, self.S, self.H, self.D = B, S, h, D
+        g = torch.Generator(device=dev).manual_seed(3000 + rank)
+        mk = lambda: torch.randn(B, S, h, D, device=dev, generator=g).to(torch.bfloat16)  # noqa: E731
+        self.qs, self.ks, self.vs = mk(), mk(), mk()
+        self.q, self.k, self.v = (t.transpose(1, 2) for t in (self.qs, self.ks, self.vs))
+        self.flop_gateup = self.flop_step = 4.0 * B * h * S * S * D / 2
+        self.launches_per_step = 1
+        self.config = {"workload": f"fmha causal bf16 B=8 H=32 S=4096 D=128 [B,S,H,D]; {h} heads per GPU",
+                       "parallelism": f"heads/{world}", "l2": "q,k,v 0.8 GB > L2"}
+
+    def step(self, ev=None):
+        if ev is not None:
+            ev[0].record()
+        out = self.ops.fmha_fwd(self.q, self.k, self.v, None, self.D ** -0.5, 1)
+        if ev is not None:
+            ev[1].record()
+        return out
+
+    def e2e_setup(self):
+        from evocompile_b200.kernels import fused_sdpa
+
+        fused_sdpa.register()
+        self.api = fused_sdpa
+        self.host = [t.cpu().pin_memory() for t in (self.qs, self.ks, self.vs)]
+        self.dev = [torch.empty_like(t) for t in (self.qs, self.ks, self.vs)]
+        self.out_host = torch.empty(self.B, self.H, self.S, self.D, dtype=torch.bfloat16).pin_memory()
+        return sum(t.numel() * 2 for t in self.host), self.out_host.numel() * 2
+
+    def e2e_step(self):
+        for d, h in zip(self.dev, self.host):
+            d.copy_(h, non_blocking=True)
+        q, k, v = (t.transpose(1, 2) for t in self.dev)
+        out = self.api.fused_attention(q, k, v, None, self.D ** -0.5, 1)
+        self.out_host.copy_(out, non_blocking=True)
+
+    def torch_reference(self):
+        import torch.nn.functional as F
+
+        return (lambda q, k, v: F.scaled_dot_product_attention(q, k, v, is_causal=True)), (self.q, self.k, self.v)
+
+    def cpu_sample(self):
+        import oracle
+
+        q, k, v = (t[:1, :4].float().cpu() for t in (self.q, self.k, self.v))
+        return (lambda: oracle.attention(q, k, v, None, self.D ** -0.5, 1)), 4.0 * 4 * self.S * self.S * self.D / 2, \
+            "1 batch x 4 heads of the causal attention (fp32 oracle)"
+
+
+class FmhaVarlen(SwigluMLP):
+    name = "fmha_varlen"
+    dominant = "fmha_varlen_fwd"
+
+    def __init__(self, dev, world, rank):
+        from evocompile_b200 import ops, shard
+
+        self.ops = ops
+        gl = torch.Generator().manual_seed(0)
+        lens_all = torch.randint(512, 8193, (16,), generator=gl).tolist()
+        mine = shard.balance_sequences(lens_all, world)[rank]
+        self.lens = [lens_all[i] for i in mine]
+        self.cu = torch.tensor(shard.cu_seqlens(self.lens), dtype=torch.int32, device=dev)
+        T = int(sum(self.lens))
+        g = torch.Generator(device=dev).manual_seed(4000 + rank)
+        self.q = torch.randn(T, 64, 128, device=dev, generator=g).to(torch.bfloat16)
+        self.k = torch.randn(T, 8, 128, device=dev, generator=g).to(torch.bfloat16)
+        self.v = torch.randn(T, 8, 128, device=dev, generator=g).to(torch.bfloat16)
+        self.flop_gateup = self.flop_step = float(sum(2 * 64 * 128 * L * L for L in self.lens))
+        self.launches_per_step = 1
+        self.config = {"workload": "fmha varlen causal GQA bf16 Hq=64 Hkv=8 D=128, 16 seqs L~U[512,8192] seed 0",
+                       "tokens_this_rank": T, "seqs_this_rank": len(self.lens),
+                       "parallelism": f"sequences/{world} token-balanced", "l2": "q,k,v > L2"}
+
+    def step(self, ev=None):
+        if ev is not None:
+            ev[0].record()
+        out = self.ops.fmha_varlen_fwd(self.q, self.k, self.v, self.cu, self.cu, max(self.lens), max(self.lens),
+                                       128 ** -0.5, 1)
+        if ev is not None:
+            ev[1].record()
+        return out
+
+    def e2e_setup(self):
+        from evocompile_b200.kernels import fused_sdpa
+
+        fused_sdpa.register()
+        self.host = [t.cpu().pin_memory() for t in (self.q, self.k, self.v)]
+        self.dev = [torch.empty_like(t) for t in (self.q, self.k, self.v)]
+        self.out_host = torch.empty(self.q.shape, dtype=torch.bfloat16).pin_memory()
+        return sum(t.numel() * 2 for t in self.host), self.out_host.numel() * 2
+
+    def e2e_step(self):
+        for d, h in zip(self.dev, self.host):
+            d.copy_(h, non_blocking=True)
+        out, _ = torch.ops.gko.fmha_varlen_fwd(*self.dev, self.cu, self.cu, max(self.lens), max(self.lens),
+                                               128 ** -0.5, 1)
+        self.out_host.copy_(out, non_blocking=True)
+
+    def torch_reference(self):
+        return None, None
+
+    def cpu_sample(self):
+        import oracle
+
+        L = min(self.lens)
+        cu = torch.tensor([0, L], dtype=torch.int32)
+        q, k, v = (t[:L].float().cpu() for t in (self.q, self.k, self.v))
+        return (lambda: oracle.attention_varlen(q, k, v, cu, cu, 128 ** -0.5, 1)), 2.0 * 64 * 128 * L * L, \
+            f"the shortest sequence (L={L}) of this rank (fp32 oracle)"
+
+
+WORKLOADS = {c.name: c for c in (SwigluMLP, AddmmGelu, FmhaCausal, FmhaVarlen)}
+
+
+# --------------------------------------------------------------------------- arms
+def time_cpu(fn, flops, budget_s=10.0, max_reps=20):
+    fn()  # warm
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < max_reps and (reps == 0 or time.perf_counter() - t0 < budget_s):
+        fn()
+        reps += 1
+    dt = (time.perf_counter() - t0) / reps
+    return flops / dt / 1e12, dt, reps
+
+
+def run_reference(args):
+    """The reference's eager path restated on the host CPU cores (rank 0 only)."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    torch.set_num_threads(os.cpu_count() or 1)
+    wl_cls = WORKLOADS[args.workload]
+    # built on the CPU from the same seeds; nothing of this arm touches the GPU
+    wl = wl_cls(torch.device("cpu"), 1, 0)
+    fn, flops, sample = wl.cpu_sample()
+    for _ in range(max(args.warmup, 0)):
+        fn()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * sum(times) / len(times)
+    value = flops / (ms / 1e3) / 1e12
+    cores = torch.get_num_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": dict(wl.config, sample=sample),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    world, rank, local = dist_setup()
+    if world != args.gpus and rank == 0:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from evocompile_b200 import _lib
+
+    _lib.load()
+    wl = WORKLOADS[args.workload](dev, world, rank)
+    stream = torch.cuda.current_stream(dev)
+
+    for _ in range(args.warmup):
+        wl.step()
+    torch.cuda.synchronize(dev)
+    assert _lib.read_status(dev) == 0, "kernel timeout during warm-up"
+
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for i in range(args.steps):
+            wl.step(kev[i])
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms_local = e0.elapsed_time(e1) / args.steps
+    kern_ms_local = sum(a.elapsed_time(b) for a, b in kev) / args.steps
+    ms = max_over_ranks(ms_local, world)
+    kern_ms = max_over_ranks(kern_ms_local, world)
+    status = _lib.read_status(dev)
+
+    # end to end through the public op API
+    h2d, d2h = wl.e2e_setup()
+    for _ in range(max(2, args.warmup)):
+        wl.e2e_step()
+    torch.cuda.synchronize(dev)
+    e2e_steps = max(5, min(args.steps, 50))
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(e2e_steps):
+        wl.e2e_step()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e2e_ms = max_over_ranks(a.elapsed_time(b) / e2e_steps, world)
+
+    # torch comparators on the same GPU (N = 1 only)
+    comparators = {}
+    if world == 1 and not args.no_compare:
+        fn, fargs = wl.torch_reference()
+        if fn is not None:
+            for name, f in (("torch_eager", fn), ("torch_compile", None)):
+                try:
+                    if name == "torch_compile":
+                        f = torch.compile(fn)
+                    for _ in range(3):
+                        f(*fargs)
+                    torch.cuda.synchronize(dev)
+                    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    n = 20
+                    x0.record(stream)
+                    for _ in range(n):
+                        f(*fargs)
+                    x1.record(stream)
+                    torch.cuda.synchronize(dev)
+                    t = x0.elapsed_time(x1) / n
+                    comparators[name] = {"ms_per_step": t, "tflops": wl.flop_step / t / 1e9}
+                except Exception as e:  # noqa: BLE001
+                    comparators[name] = {"error": repr(e)[:200]}
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu:
+        torch.set_num_threads(os.cpu_count() or 1)
+        fn, flops, sample = wl.cpu_sample()
+        tf, dt, reps = time_cpu(fn, flops)
+        cpu = {"value": tf, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": f"{sample}; {reps} reps, {dt * 1e3:.1f} ms each"}
+
+    if rank == 0:
+        pk, pk_src = peaks()
+        peak = pk["bf16_tflops"]
+        value = world * wl.flop_step / (ms / 1e3) / 1e12
+        achieved = wl.flop_gateup / (kern_ms / 1e3) / 1e12
+        traffic = traffic_per_launch(wl.dominant)
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": wl.config,
+            "pct_of_peak": value / (world * peak),
+            "roofline": {"bound": "tensor", "kernel": wl.dominant, "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{pk_src} bf16 burst (MEASURED_PEAKS.json)" if pk_src == "measured"
+                         else "fallback 1590 TFLOP/s", "flop_per_launch": wl.flop_gateup,
+                         "avg_launch_ms": kern_ms},
+            "cpu_baseline": cpu,
+            "e2e": {"value": world * wl.flop_step / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "gpu_launches": wl.launches_per_step * args.steps,
+            "clocks": clocks.summary(),
+            "comparators": comparators or None,
+            "kernel_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="swiglu")
+    ap.add_argument("--no-compare", action="store_true", help="skip the torch eager / torch.compile comparators")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -162,8 +162,8 @@ extern "C" int gko_addmm_act(int dtype, int act, int64_t m, int64_t n, int64_t k
   if (act != GKO_ACT_NONE && act != GKO_ACT_GELU && act != GKO_ACT_RELU)
     return fail(GKO_ERR_INVALID, "unknown activation code %d", act);
   if (m < 0 || n < 0 || k < 0) return fail(GKO_ERR_INVALID, "negative GEMM size");
-  if ((m && n && (!d)) || (m && k && !a) || (n && k && !b))
-    return fail(GKO_ERR_INVALID, "null operand pointer");
+  if (m == 0 || n == 0) return GKO_OK;  // empty output: nothing is read or written
+  if (!d || (k && (!a || !b))) return fail(GKO_ERR_INVALID, "null operand pointer");
   const int bk = bias_kind_of(bias, bias_dtype);
   if (bk < 0) return fail(GKO_ERR_INVALID, "unknown bias dtype code %d", bias_dtype);
   const int epi = act == GKO_ACT_GELU ? kEpiGelu : act == GKO_ACT_RELU ? kEpiRelu : kEpiNone;
@@ -193,8 +193,8 @@ extern "C" int gko_linear_swiglu(int dtype, int64_t m, int64_t h, int64_t k, con
                                  void* stream) {
   if (host::dtype_size(dtype) == 0) return fail(GKO_ERR_INVALID, "unknown dtype code %d", dtype);
   if (m < 0 || h < 0 || k < 0) return fail(GKO_ERR_INVALID, "negative GEMM size");
-  if ((m && h && !out) || (m && k && !x) || (h && k && !w))
-    return fail(GKO_ERR_INVALID, "null operand pointer");
+  if (m == 0 || h == 0) return GKO_OK;  // empty output: nothing is read or written
+  if (!out || (k && (!x || !w))) return fail(GKO_ERR_INVALID, "null operand pointer");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (m == 0 || h == 0) return GKO_OK;
   if (dtype == GKO_F32)

@@ -132,8 +132,12 @@ def swiglu_mlp(x, w_gate_up, w_down):
 def silu_mul(x, y):
     """silu(x) * y elementwise (gko::silu_mul, eval/kernels/silu_mul.py:29-43)."""
     dev = _lib.require_cuda(x, y)
-    if x.shape != y.shape or x.dtype != y.dtype:
-        raise RuntimeError(f"silu_mul: operands differ: {tuple(x.shape)} {x.dtype} vs {tuple(y.shape)} {y.dtype}")
+    if x.dtype != y.dtype:
+        raise RuntimeError(f"silu_mul: dtypes differ: {x.dtype} vs {y.dtype}")
+    if x.shape != y.shape:
+        # broadcasting operands (e.g. an SE gate [B, C, 1, 1]) are expanded to the result shape
+        shape = torch.broadcast_shapes(x.shape, y.shape)
+        x, y = x.expand(shape), y.expand(shape)
     xc = x.contiguous()
     yc = y.contiguous()
     out = torch.empty_like(xc)

@@ -1,0 +1,100 @@
+"""The C ABI on a machine without a GPU: libgko_b200.so loads, exports every
+function include/gko_b200.h declares, and rejects bad arguments before any
+CUDA call with the documented error codes and messages."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from evocompile_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "gko_b200.h"
+
+
+def _declared():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(gko_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    for n in ("gko_addmm_act", "gko_linear_swiglu", "gko_fmha_fwd", "gko_fmha_varlen_fwd", "gko_silu_mul",
+              "gko_last_error", "gko_version"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in _declared():
+        assert hasattr(lib, name), f"{name} declared in gko_b200.h but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_version(lib):
+    assert lib.gko_version() >= 100
+
+
+def _null():
+    return ctypes.c_void_p(0)
+
+
+def test_addmm_rejects_unknown_dtype(lib):
+    rc = lib.gko_addmm_act(99, 1, 4, 4, 4, _null(), 4, 1, _null(), 1, 4, _null(), 0, _null(), 4, _null(), _null())
+    assert rc == _lib.ERR_INVALID
+    assert "dtype" in _lib.last_error()
+
+
+def test_addmm_rejects_unknown_activation(lib):
+    rc = lib.gko_addmm_act(_lib.BF16, 7, 4, 4, 4, _null(), 4, 1, _null(), 1, 4, _null(), 0, _null(), 4, _null(), _null())
+    assert rc == _lib.ERR_INVALID and "activation" in _lib.last_error()
+
+
+def test_addmm_rejects_negative_and_null(lib):
+    assert lib.gko_addmm_act(_lib.BF16, 1, -1, 4, 4, _null(), 4, 1, _null(), 1, 4, _null(), 0, _null(), 4,
+                             _null(), _null()) == _lib.ERR_INVALID
+    assert lib.gko_addmm_act(_lib.BF16, 1, 4, 4, 4, _null(), 4, 1, _null(), 1, 4, _null(), 0, _null(), 4,
+                             _null(), _null()) == _lib.ERR_INVALID
+    assert "null" in _lib.last_error()
+
+
+def test_empty_gemm_is_a_no_op(lib):
+    assert lib.gko_addmm_act(_lib.BF16, 1, 0, 4, 4, _null(), 4, 1, _null(), 1, 4, _null(), 0, _null(), 4,
+                             _null(), _null()) == _lib.OK
+
+
+def test_tensor_core_layout_constraints(lib):
+    fake = ctypes.c_void_p(1 << 20)  # never dereferenced: validation fails first
+    # K % 8 != 0 -> unsupported (stride rule of the TMA descriptors)
+    rc = lib.gko_addmm_act(_lib.BF16, 1, 16, 16, 12, fake, 12, 1, fake, 1, 12, _null(), 0, fake, 16, _null(), _null())
+    assert rc == _lib.ERR_UNSUPPORTED and "multiples of 8" in _lib.last_error()
+    # mat1 not row-major
+    rc = lib.gko_addmm_act(_lib.BF16, 1, 16, 16, 16, fake, 1, 16, fake, 1, 16, _null(), 0, fake, 16, _null(), _null())
+    assert rc == _lib.ERR_UNSUPPORTED and "row-major" in _lib.last_error()
+
+
+def _i64x4(*v):
+    return (ctypes.c_int64 * 4)(*v)
+
+
+def test_fmha_rejects_head_dim_and_dtype(lib):
+    st = _i64x4(0, 0, 0, 1)
+    args = lambda dt, d, hq=4, hkv=2: (dt, 1, hq, hkv, 16, 16, d, _null(), st, _null(), st, _null(), st, _null(), 0, 0,
+                                      st, 1, 0.1, 0, 0, 0.0, _null(), _null(), _null(), _null())
+    assert lib.gko_fmha_fwd(*args(_lib.BF16, 96)) == _lib.ERR_UNSUPPORTED
+    assert "head dim" in _lib.last_error()
+    assert lib.gko_fmha_fwd(*args(_lib.F32, 64)) == _lib.ERR_UNSUPPORTED
+    assert lib.gko_fmha_fwd(*args(_lib.BF16, 64, 4, 3)) == _lib.ERR_INVALID
+    assert "multiple of kv heads" in _lib.last_error()
+
+
+def test_fmha_varlen_rejects_negative(lib):
+    rc = lib.gko_fmha_varlen_fwd(_lib.BF16, -1, 4, 4, 128, 10, 10, 10, _null(), 512, 128, _null(), 512, 128,
+                                 _null(), 512, 128, _null(), _null(), 0.1, 1, 0, 0.0, _null(), _null(), _null(), _null())
+    assert rc == _lib.ERR_INVALID
+
+
+def test_silu_mul_validation(lib):
+    assert lib.gko_silu_mul(_lib.BF16, -3, _null(), _null(), _null(), _null(), _null()) == _lib.ERR_INVALID
+    assert lib.gko_silu_mul(_lib.BF16, 0, _null(), _null(), _null(), _null(), _null()) == _lib.OK
+    assert lib.gko_silu_mul(_lib.BF16, 8, _null(), _null(), _null(), _null(), _null()) == _lib.ERR_INVALID
