@@ -54,6 +54,7 @@ SIGNATURES = {
          _i64, _vp, _vp, _fl, _int, _int, _fl, _vp, _vp, _vp, _vp],
     ),
     "gko_silu_mul": (_int, [_int, _i64, _vp, _vp, _vp, _vp, _vp]),
+    "gko_selftest_wait_timeout": (_int, [_vp, ctypes.c_longlong, _vp]),
 }
 
 

@@ -1,16 +1,23 @@
 // Fused multi-head attention forward for sm_100a (gko::fused_sdpa_pair,
 // gko::cutlass_fmha_pair, gko::fmha_varlen_fwd).
 //
-// One CTA computes a 128-row query tile of one (batch, head) against the key
-// range its masks allow, in 128-key tiles:
-//   warp 0     TMA producer: Q once, then K_j / V_j into a 2-stage ring
-//   warp 1     MMA issuer + TMEM owner: S_j = Q K_j^T into TMEM (2 buffers),
-//              O += P_j V_j into a TMEM accumulator
-//   warps 2-5  softmax: one thread per query row reads S_j from TMEM, applies
-//              scale / bias / softcap / masks, keeps the running max and sum,
-//              writes P_j (bf16/f16) to shared memory, rescales O in TMEM only
-//              when the running max grows by more than 2^8, and finally
-//              normalises O and writes out / lse.
+// One CTA computes a 256-row query block (two 128-row tiles Q0, Q1) of one
+// (batch, head) against the key range the masks allow, in 128-key tiles:
+//   warp 8     TMA producer: Q0/Q1 once, then K_j / V_j into a 2-stage ring
+//   warp 9     MMA issuer + TMEM owner. Per key tile j and query tile t it issues
+//              S_t = Q_t K_j^T into TMEM, then (once softmax has written P_t)
+//              O_t += P_t V_j with P_t read from TMEM (the TS form of tcgen05.mma),
+//              then S_t for tile j+1 — so the tensor core works on one query tile
+//              while the other tile's softmax runs.
+//   warps 0-3  softmax of Q0, warps 4-7 softmax of Q1: one thread per query row
+//              reads S_t from TMEM, applies scale / bias / softcap / masks, keeps
+//              the running max and sum, writes P_t (bf16/f16) back into the S_t
+//              columns, rescales O_t in TMEM only when the running max grows by
+//              more than 2^8, and at the end normalises O_t and writes out / lse.
+// TMEM (512 columns): S0|P0 [0,128), S1|P1 [128,256), O0 [256,256+D), O1 [384,384+D).
+// Registers: the CTA launches with 12 x 32 threads x 168 registers; the
+// producer/MMA warpgroup (warps 8-11) drops to 56 registers per thread and the two
+// softmax warpgroups rise to 216 (2 x 128 x 216 + 128 x 56 = 62464 <= 64512).
 // Semantics follow the reference Triton kernel _flash_fwd
 // (eval/kernels/fused_sdpa.py:25-157): logits = scale * q.k (+ bias), then
 // softcap, then masks (key padding, causal key <= query, |key - query| <= window);
@@ -23,9 +30,16 @@
 namespace gko {
 namespace fmha {
 
-constexpr int kBM = 128;
-constexpr int kBN = 128;
-constexpr int kThreads = 192;
+constexpr int kBM = 128;           // rows of one query tile
+constexpr int kQTiles = 2;         // query tiles per CTA
+constexpr int kBlockM = kBM * kQTiles;
+constexpr int kBN = 128;           // keys per tile
+constexpr int kThreads = 384;      // 2 x 4 softmax warps, producer, MMA, 2 idle
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr uint32_t kRegsSoftmax = 216;
+constexpr uint32_t kRegsControl = 56;
+static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsControl <= 384 * 168, "register split exceeds the launch");
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -34,7 +48,7 @@ constexpr float kRescaleThreshold = 8.f;  // log2 units
 struct Params {
   int hq, hkv, group;  // group = hq / hkv
   int sq, sk;          // dense: per-batch lengths; varlen: unused
-  int q_tiles;         // tiles along the query axis (grid.y)
+  int q_tiles;         // 256-row query blocks along the query axis (grid.y)
   float scale, scale_log2, softcap;
   int causal, window;
   // bias (dense only)
@@ -56,11 +70,10 @@ struct Layout {
   static constexpr uint32_t kChunk = 128 * 128;  // one [128 rows x 128 B] swizzle block
   static constexpr int kChunks = D / 64;
   static constexpr uint32_t kTile = kChunks * kChunk;  // 128 x D elements
-  static constexpr uint32_t kQ = 0;
-  static constexpr uint32_t kK0 = kQ + kTile;
-  static constexpr uint32_t kV0 = kK0 + 2 * kTile;
-  static constexpr uint32_t kP = kV0 + 2 * kTile;
-  static constexpr uint32_t kMeta = kP + 2 * kChunk;
+  static constexpr uint32_t kQ = 0;                 // Q0, Q1
+  static constexpr uint32_t kK0 = kQ + 2 * kTile;   // K stages 0, 1
+  static constexpr uint32_t kV0 = kK0 + 2 * kTile;  // V stages 0, 1
+  static constexpr uint32_t kMeta = kV0 + 2 * kTile;
   // at least 120 KB so that a single CTA (and its 512 TMEM columns) occupies an SM
   static constexpr uint32_t kBytes = (1024 + kMeta + 256) > 122880 ? (1024 + kMeta + 256) : 122880;
 };
@@ -83,12 +96,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kIdescS = make_idesc_f16(kBF16, kBM, kBN, false, false);
   constexpr uint32_t kIdescO = make_idesc_f16(kBF16, kBM, D, false, true);
 
-  // ---------------------------------------------------------- tile geometry
+  // ---------------------------------------------------------- block geometry
   const int bh = blockIdx.x;
   const int h = bh % p.hq;
   const int zb = bh / p.hq;  // batch (dense) or sequence (varlen)
-  const int qt = p.q_tiles - 1 - (int)blockIdx.y;  // heaviest (causal) tiles first
-  const int m0 = qt * kBM;
+  const int qb = p.q_tiles - 1 - (int)blockIdx.y;  // heaviest (causal) blocks first
+  const int m0 = qb * kBlockM;
   int len_q, len_k, row_q0, row_k0;
   if constexpr (VARLEN) {
     row_q0 = p.cu_q[zb];
@@ -105,15 +118,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int hk = h / p.group;
   const int zc = VARLEN ? 0 : zb;  // tensor-map batch coordinate
 
-  // key range this query tile can see
-  int k_lo = 0, k_hi = len_k;
-  if (p.causal) k_hi = min(k_hi, m0 + kBM);
-  if (p.window > 0) {
-    k_lo = max(k_lo, m0 - p.window);
-    k_hi = min(k_hi, m0 + kBM + p.window);
+  // key-tile range [lo_t, hi_t) of each query tile (empty when the tile is past the end)
+  int lo_t[kQTiles], hi_t[kQTiles];
+#pragma unroll
+  for (int t = 0; t < kQTiles; ++t) {
+    const int mt = m0 + t * kBM;
+    int k_lo = 0, k_hi = len_k;
+    if (p.causal) k_hi = min(k_hi, mt + kBM);
+    if (p.window > 0) {
+      k_lo = max(k_lo, mt - p.window);
+      k_hi = min(k_hi, mt + kBM + p.window);
+    }
+    if (mt >= len_q || k_hi <= k_lo) {
+      lo_t[t] = hi_t[t] = 0;
+    } else {
+      lo_t[t] = k_lo / kBN;
+      hi_t[t] = (k_hi + kBN - 1) / kBN;
+    }
   }
-  const int t_lo = k_lo / kBN;
-  const int n_tiles = (k_hi > k_lo) ? ((k_hi + kBN - 1) / kBN - t_lo) : 0;
+  int lo = 1 << 30, hi = 0;
+#pragma unroll
+  for (int t = 0; t < kQTiles; ++t)
+    if (hi_t[t] > lo_t[t]) {
+      lo = min(lo, lo_t[t]);
+      hi = max(hi, hi_t[t]);
+    }
+  const int n_tiles = hi > lo ? hi - lo : 0;
 
   // ---------------------------------------------------------- shared memory
   extern __shared__ uint8_t smem_raw[];
@@ -123,14 +153,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* meta = smem_raw + pad + L::kMeta;
   const uint32_t smeta = sb + L::kMeta;
   const uint32_t bar_q = smeta;
-  const uint32_t bar_kfull = smeta + 8;    // [2]
-  const uint32_t bar_kempty = smeta + 24;  // [2]
-  const uint32_t bar_vfull = smeta + 40;   // [2]
-  const uint32_t bar_vempty = smeta + 56;  // [2]
-  const uint32_t bar_sfull = smeta + 72;   // [2]
-  const uint32_t bar_sfree = smeta + 88;   // [2]
-  const uint32_t bar_pfull = smeta + 104;
-  const uint32_t bar_odone = smeta + 112;
+  const uint32_t bar_kfull = smeta + 8;     // [2]
+  const uint32_t bar_kempty = smeta + 24;   // [2]
+  const uint32_t bar_vfull = smeta + 40;    // [2]
+  const uint32_t bar_vempty = smeta + 56;   // [2]
+  const uint32_t bar_sfull = smeta + 72;    // [2] per query tile
+  const uint32_t bar_pfull = smeta + 88;    // [2] per query tile
+  const uint32_t bar_ofinal = smeta + 104;  // [2] per query tile
   const uint32_t bar_drain = smeta + 120;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 128);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 132);
@@ -146,10 +175,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_vfull + 8 * i, 1);
       mbar_init(bar_vempty + 8 * i, 1);
       mbar_init(bar_sfull + 8 * i, 1);
-      mbar_init(bar_sfree + 8 * i, 4);
+      mbar_init(bar_pfull + 8 * i, 4);
+      mbar_init(bar_ofinal + 8 * i, 1);
     }
-    mbar_init(bar_pfull, 4);
-    mbar_init(bar_odone, 1);
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -157,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tm_k);
     prefetch_tmap(&tm_v);
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
@@ -165,19 +193,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const uint32_t tmem_o = tmem_base + 256;
 
-  if (warp == 0) {
+  // Each role's code is dominated by its warpgroup's setmaxnreg (no join in between),
+  // so the compiler allocates the softmax code against 216 registers.
+  if (warp >= kProducerWarp) {
+  setmaxnreg_dec<kRegsControl>();
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0 && n_tiles > 0) {
-      mbar_arrive_expect_tx(bar_q, L::kTile);
+      mbar_arrive_expect_tx(bar_q, kQTiles * L::kTile);
 #pragma unroll
-      for (int c = 0; c < L::kChunks; ++c)
-        tma_load_4d(sb + L::kQ + c * L::kChunk, &tm_q, bar_q, c * 64, row_q0 + m0, h, zc);
-      for (int i = 0; i < n_tiles; ++i) {
-        const int st = i & 1;
-        const uint32_t ph = (i >> 1) & 1;
-        const int krow = row_k0 + (t_lo + i) * kBN;
+      for (int t = 0; t < kQTiles; ++t)
+#pragma unroll
+        for (int c = 0; c < L::kChunks; ++c)
+          tma_load_4d(sb + L::kQ + t * L::kTile + c * L::kChunk, &tm_q, bar_q, c * 64,
+                      row_q0 + m0 + t * kBM, h, zc);
+      for (int u = 0; u < n_tiles; ++u) {
+        const int st = u & 1;
+        const uint32_t ph = (u >> 1) & 1;
+        const int krow = row_k0 + (lo + u) * kBN;
         if (!wait_bounded(bar_kempty + 8 * st, ph ^ 1, abort_flag, p.status, kStatusTimeoutProducer))
           break;
         mbar_arrive_expect_tx(bar_kfull + 8 * st, L::kTile);
@@ -194,70 +228,92 @@ __global__ void __launch_bounds__(kThreads, 1)
                       krow, hk, zc);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && n_tiles > 0) {
       bool ok = wait_bounded(bar_q, 0, abort_flag, p.status, kStatusTimeoutMma);
-      auto issue_pv = [&](int i) -> bool {
-        const int st = i & 1;
-        if (!wait_bounded(bar_pfull, i & 1, abort_flag, p.status, kStatusTimeoutMma)) return false;
-        if (!wait_bounded(bar_vfull + 8 * st, (i >> 1) & 1, abort_flag, p.status, kStatusTimeoutMma))
-          return false;
-        tc_fence_after();
-        const uint32_t v_addr = sb + L::kV0 + st * L::kTile;
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t adesc =
-              make_sdesc_sw128(sb + L::kP + (kk >> 2) * L::kChunk + (kk & 3) * 32, 16, 1024);
-          const uint64_t bdesc = make_sdesc_sw128(v_addr + kk * 16 * 128, L::kChunk, 1024);
-          mma_f16_ss(tmem_o, adesc, bdesc, kIdescO, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(bar_odone);
-        mma_commit(bar_vempty + 8 * st);
-        return true;
-      };
-      for (int i = 0; i < n_tiles && ok; ++i) {
-        const int st = i & 1;
-        if (!wait_bounded(bar_kfull + 8 * st, (i >> 1) & 1, abort_flag, p.status, kStatusTimeoutMma) ||
-            !wait_bounded(bar_sfree + 8 * st, ((i >> 1) & 1) ^ 1, abort_flag, p.status,
-                          kStatusTimeoutMma)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
+      auto issue_s = [&](int t, int u) {
+        const int st = u & 1;
         const uint32_t k_addr = sb + L::kK0 + st * L::kTile;
-        const uint32_t s_tmem = tmem_base + st * kBN;
+        const uint32_t q_addr = sb + L::kQ + t * L::kTile;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * L::kChunk + (kk & 3) * 32;
-          const uint64_t adesc = make_sdesc_sw128(sb + L::kQ + off, 16, 1024);
-          const uint64_t bdesc = make_sdesc_sw128(k_addr + off, 16, 1024);
-          mma_f16_ss(s_tmem, adesc, bdesc, kIdescS, kk > 0 ? 1u : 0u);
+          mma_f16_ss(tmem_base + t * kBN, make_sdesc_sw128(q_addr + off, 16, 1024),
+                     make_sdesc_sw128(k_addr + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
         }
-        mma_commit(bar_sfull + 8 * st);
-        mma_commit(bar_kempty + 8 * st);
-        if (i >= 1 && !issue_pv(i - 1)) ok = false;
+        mma_commit(bar_sfull + 8 * t);
+      };
+      auto issue_pv = [&](int t, int u, bool first) {
+        const int st = u & 1;
+        const uint32_t v_addr = sb + L::kV0 + st * L::kTile;
+        const uint32_t o_tmem = tmem_base + 256 + t * 128;
+        const uint32_t p_tmem = tmem_base + t * kBN;
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          mma_f16_ts(o_tmem, p_tmem + kk * 8, make_sdesc_sw128(v_addr + kk * 16 * 128, L::kChunk, 1024),
+                     kIdescO, (!first || kk > 0) ? 1u : 0u);
+      };
+      // prologue: S_t for the first key tile
+      if (ok) ok = wait_bounded(bar_kfull, 0, abort_flag, p.status, kStatusTimeoutMma);
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int t = 0; t < kQTiles; ++t)
+          if (lo >= lo_t[t] && lo < hi_t[t]) issue_s(t, 0);
+        mma_commit(bar_kempty);
       }
-      if (ok) ok = issue_pv(n_tiles - 1);
+      for (int u = 0; u < n_tiles && ok; ++u) {
+        const int j = lo + u;
+        const int st = u & 1;
+        const uint32_t ph = (u >> 1) & 1;
+        ok = wait_bounded(bar_vfull + 8 * st, ph, abort_flag, p.status, kStatusTimeoutMma);
+        const bool next = (u + 1 < n_tiles);
+        if (ok && next)
+          ok = wait_bounded(bar_kfull + 8 * ((u + 1) & 1), ((u + 1) >> 1) & 1, abort_flag, p.status,
+                            kStatusTimeoutMma);
+        if (!ok) break;
+#pragma unroll
+        for (int t = 0; t < kQTiles && ok; ++t) {
+          if (j >= lo_t[t] && j < hi_t[t]) {
+            ok = wait_bounded(bar_pfull + 8 * t, (j - lo_t[t]) & 1, abort_flag, p.status, kStatusTimeoutMma);
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv(t, u, j == lo_t[t]);
+            if (j == hi_t[t] - 1) mma_commit(bar_ofinal + 8 * t);
+          }
+          if (next && j + 1 >= lo_t[t] && j + 1 < hi_t[t]) issue_s(t, u + 1);
+        }
+        if (!ok) break;
+        mma_commit(bar_vempty + 8 * st);
+        if (next) mma_commit(bar_kempty + 8 * ((u + 1) & 1));
+      }
       if (*abort_flag) {
         mma_commit(bar_drain);
         wait_for(bar_drain, 0, p.status, kStatusTimeoutDrain);
       }
     }
+  }
   } else {
+    setmaxnreg_inc<kRegsSoftmax>();
     // ------------------------------------------------------------ softmax / epilogue
-    const int quarter = warp & 3;
+    const int t = warp >> 2;            // query tile of this warpgroup
+    const int quarter = warp & 3;       // TMEM lane quarter
     const int r = quarter * 32 + lane;  // query row within the tile
-    const int qi = m0 + r;              // query index within the sequence
+    const int qi = m0 + t * kBM + r;    // query index within the sequence
     const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_tmem = tmem_base + lane_off + t * kBN;
+    const uint32_t o_tmem = tmem_base + lane_off + 256 + t * 128;
+    const int jlo = t ? lo_t[1] : lo_t[0];
+    const int jhi = t ? hi_t[1] : hi_t[0];
+    const int mt = m0 + t * kBM;
     float m_run = -INFINITY;  // running max, log2 domain
     float l_run = 0.f;
     bool ok = true;
-    for (int i = 0; i < n_tiles; ++i) {
-      const int st = i & 1;
-      const int kbase = (t_lo + i) * kBN;
-      if (!wait_bounded(bar_sfull + 8 * st, (i >> 1) & 1, abort_flag, p.status,
-                        kStatusTimeoutSoftmax)) {
+    for (int j = jlo; j < jhi; ++j) {
+      const int i = j - jlo;
+      const int kbase = j * kBN;
+      if (!wait_bounded(bar_sfull + 8 * t, i & 1, abort_flag, p.status, kStatusTimeoutSoftmax)) {
         ok = false;
         break;
       }
@@ -266,41 +322,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         uint32_t su[kBN];
 #pragma unroll
-        for (int c = 0; c < kBN / 32; ++c) tmem_ld32p(tmem_base + lane_off + st * kBN + c * 32, su + c * 32);
+        for (int c = 0; c < kBN / 32; ++c) tmem_ld32p(s_tmem + c * 32, su + c * 32);
         tmem_wait_ld();
 #pragma unroll
         for (int c = 0; c < kBN; ++c) s[c] = __uint_as_float(su[c]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_sfree + 8 * st);
-
       // logits in the log2 domain
-      const bool need_mask = (kbase + kBN > len_k) || (p.causal && kbase + kBN - 1 > m0);
       float tmax = -INFINITY;
       if constexpr (EXTRA) {
 #pragma unroll
         for (int c = 0; c < kBN; ++c) {
           const int kj = kbase + c;
-          float t = s[c] * p.scale;
-          if (p.bias_mode != GKO_BIAS_NONE && kj < len_k && qi < len_q) t += bias_value(p, zb, h, qi, kj);
-          if (p.softcap > 0.f) {
-            float x = fminf(fmaxf(t / p.softcap, -15.f), 15.f);
-            t = p.softcap * tanhf(x);
-          }
+          float x = s[c] * p.scale;
+          if (p.bias_mode != GKO_BIAS_NONE && kj < len_k && qi < len_q) x += bias_value(p, zb, h, qi, kj);
+          if (p.softcap > 0.f) x = p.softcap * tanhf(fminf(fmaxf(x / p.softcap, -15.f), 15.f));
           bool keep = kj < len_k;
           if (p.causal) keep = keep && (kj <= qi);
           if (p.window > 0) keep = keep && (kj - qi <= p.window) && (qi - kj <= p.window);
-          s[c] = keep ? t * kLog2e : -INFINITY;
+          s[c] = keep ? x * kLog2e : -INFINITY;
           tmax = fmaxf(tmax, s[c]);
         }
       } else {
+        const bool need_mask = (kbase + kBN > len_k) || (p.causal && kbase + kBN - 1 > mt);
         if (need_mask) {
 #pragma unroll
           for (int c = 0; c < kBN; ++c) {
             const int kj = kbase + c;
-            bool keep = kj < len_k;
-            if (p.causal) keep = keep && (kj <= qi);
+            const bool keep = (kj < len_k) && (!p.causal || kj <= qi);
             s[c] = keep ? s[c] * p.scale_log2 : -INFINITY;
             tmax = fmaxf(tmax, s[c]);
           }
@@ -315,60 +363,49 @@ __global__ void __launch_bounds__(kThreads, 1)
       // lazy rescale: keep the old max unless the new one exceeds it by the threshold
       float m_new = m_run;
       float alpha = 1.f;
-      if (tmax > m_run + kRescaleThreshold || (m_run == -INFINITY && tmax > -INFINITY)) {
+      if (tmax > m_run + kRescaleThreshold) {
         m_new = tmax;
         alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_new);
       }
+      // O_t is stable here: S_t(j) completing implies PV_t(j-1) (issued before it) completed.
+      if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(o_tmem + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(o_tmem + c * 32, o);
+        }
+      }
+      // P_t (bf16/f16 pairs) into the first kBN/2 columns of the S_t region, 64 keys at a time
       const float m_sub = (m_new == -INFINITY) ? 0.f : m_new;
       float rsum = 0.f;
-      uint32_t pk[kBN / 2];
 #pragma unroll
-      for (int c = 0; c < kBN / 2; ++c) {
-        const float p0 = fast_exp2(s[2 * c] - m_sub);
-        const float p1 = fast_exp2(s[2 * c + 1] - m_sub);
-        rsum += p0 + p1;
-        pk[c] = Cvt<T>::pack(p0, p1);
-      }
-      // P buffer and O are free once PV_{i-1} has completed
-      if (i > 0) {
-        if (!wait_bounded(bar_odone, (i - 1) & 1, abort_flag, p.status, kStatusTimeoutSoftmax)) {
-          ok = false;
-          break;
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float p0 = fast_exp2(s[half * 64 + 2 * c] - m_sub);
+          const float p1 = fast_exp2(s[half * 64 + 2 * c + 1] - m_sub);
+          rsum += p0 + p1;
+          pk[c] = Cvt<T>::pack(p0, p1);
         }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(tmem_o + lane_off + c * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st32(tmem_o + lane_off + c * 32, o);
-          }
-          tmem_wait_st();
-        }
+        tmem_st32(s_tmem + half * 32, pk);
       }
-      // P tile (128 rows x 128 keys), K-major, 128-byte swizzle, two 64-key chunks
-#pragma unroll
-      for (int j = 0; j < kBN / 8; ++j) {
-        const int chunk = j >> 3;
-        const int piece = j & 7;
-        const uint32_t addr =
-            sb + L::kP + chunk * L::kChunk + r * 128 + ((piece ^ (r & 7)) << 4);
-        st_shared_v4(addr, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-      }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar_pfull);
+      if (lane == 0) mbar_arrive(bar_pfull + 8 * t);
       l_run = l_run * alpha + rsum;
       m_run = m_new;
     }
 
     // ---------------------------------------------------------- epilogue
-    if (ok && n_tiles > 0) {
-      ok = wait_bounded(bar_odone, (n_tiles - 1) & 1, abort_flag, p.status, kStatusTimeoutSoftmax);
+    const bool has = jhi > jlo;
+    if (ok && has) {
+      ok = wait_bounded(bar_ofinal + 8 * t, 0, abort_flag, p.status, kStatusTimeoutSoftmax);
       tc_fence_after();
     }
     const bool write = qi < len_q;
@@ -378,11 +415,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     else
       orow = reinterpret_cast<T*>(p.out) + (((int64_t)zb * p.hq + h) * p.sq + qi) * D;
     const float inv = (l_run > 0.f) ? 1.f / l_run : 0.f;
-    if (ok && n_tiles > 0) {
+    if (ok && has) {
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
-        tmem_ld32(tmem_o + lane_off + c * 32, o);
+        tmem_ld32(o_tmem + c * 32, o);
         tmem_wait_ld();
         uint32_t w[16];
 #pragma unroll
@@ -413,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+  if (warp == kMmaWarp) tmem_dealloc(tmem_base, kTmemCols);
 }
 
 // ------------------------------------------------------------------ host side
@@ -515,7 +552,7 @@ extern "C" int gko_fmha_fwd(int dtype, int64_t z, int64_t hq, int64_t hkv, int64
   p.group = (int)(hq / hkv);
   p.sq = (int)sq;
   p.sk = (int)sk;
-  p.q_tiles = (int)((sq + fmha::kBM - 1) / fmha::kBM);
+  p.q_tiles = (int)((sq + fmha::kBlockM - 1) / fmha::kBlockM);
   p.scale = scale;
   p.scale_log2 = scale * fmha::kLog2e;
   p.softcap = softcap;
@@ -581,7 +618,7 @@ extern "C" int gko_fmha_varlen_fwd(int dtype, int64_t b, int64_t hq, int64_t hkv
   p.hq = (int)hq;
   p.hkv = (int)hkv;
   p.group = (int)(hq / hkv);
-  p.q_tiles = (int)((max_seqlen_q + fmha::kBM - 1) / fmha::kBM);
+  p.q_tiles = (int)((max_seqlen_q + fmha::kBlockM - 1) / fmha::kBlockM);
   p.scale = scale;
   p.scale_log2 = scale * fmha::kLog2e;
   p.softcap = softcap;

@@ -111,6 +111,21 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
   p.n_blocks = (int)((N_out + bn - 1) / bn);
   p.num_tiles = p.m_blocks * p.n_blocks;
   p.k_blocks = (int)((K + gemm::kBK - 1) / gemm::kBK);
+  {
+    // Raster: the operand a group of tiles shares (an A row-block group, or a B column-block
+    // group) is sized to stay resident in about half of the 126 MB L2; pick the grouping
+    // axis that minimises the estimated DRAM reads of the other operand.
+    const double budget = 64.0 * 1024.0 * 1024.0;
+    const double a_bytes = (double)M * K * esz, b_bytes = (double)nb_total * K * esz;
+    const double a_blk = (double)gemm::kBM * K * esz, b_blk = (double)gemm::kMmaN * K * esz;
+    int gm = (int)(budget / a_blk), gn = (int)(budget / b_blk);
+    gm = gm < 1 ? 1 : (gm > p.m_blocks ? p.m_blocks : gm);
+    gn = gn < 1 ? 1 : (gn > p.n_blocks ? p.n_blocks : gn);
+    const double t_m = a_bytes + b_bytes * (double)((p.m_blocks + gm - 1) / gm);
+    const double t_n = b_bytes + a_bytes * (double)((p.n_blocks + gn - 1) / gn);
+    p.raster_n = t_n < t_m ? 1 : 0;
+    p.group = p.raster_n ? gn : gm;
+  }
   p.bias = bias;
   p.bias_kind = bias_kind;
   p.status = status;

@@ -9,8 +9,11 @@
 //   kEpiRelu   : D = relu(A*B^T + bias)
 //   kEpiSwiglu : D = silu(A*Bg^T) * (A*Bu^T)             gko::gemm_swiglu, B = [Bg; Bu]
 //
-// CTA = 6 warps:  warp 0 TMA producer, warp 1 MMA issuer (+TMEM owner),
-//                 warps 2..5 epilogue (TMEM -> registers -> smem -> TMA store).
+// CTA = 10 warps: warp 0 TMA producer, warp 1 MMA issuer (+TMEM owner),
+//                 warps 2..9 epilogue (TMEM -> registers -> smem -> TMA store); two
+//                 warps per TMEM lane quarter, each converting half of the columns.
+// Tile order: grouped raster chosen on the host so that the operand shared by a
+// group of tiles stays resident in L2 (see GemmParams::group / raster_n).
 // Tiles: 128 x 256 accumulator (SwiGLU: 128 gate + 128 up columns -> 128 outputs),
 // K step 64 (one 128-byte swizzle row), 4-stage smem ring, two TMEM accumulators
 // (2 x 256 columns) so the epilogue of tile i overlaps the main loop of tile i+1.
@@ -34,6 +37,8 @@ struct GemmParams {
   int n_blocks;     // ceil(N_out / kBlockNOut)
   int num_tiles;    // m_blocks * n_blocks
   int k_blocks;     // ceil(K / 64)
+  int group;        // raster: tiles sweep the other axis in groups of this many blocks
+  int raster_n;     // 0: groups of M-blocks (A group stays in L2), 1: groups of N-blocks
   const void* bias;
   int bias_kind;
   unsigned* status;
@@ -45,25 +50,31 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kMmaN = 256;
 constexpr int kStages = 4;
-constexpr int kThreads = 192;
-constexpr int kGroupM = 16;  // raster: 16 M-blocks share a sweep over N
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
 constexpr uint32_t kABytes = kBM * kBK * 2;       // 16 KB
 constexpr uint32_t kBBytes = kMmaN * kBK * 2;     // 32 KB
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
-constexpr uint32_t kStagingBytes = 4 * 2 * 32 * 128;  // 4 warps x 2 buffers x (32 rows x 128 B)
+constexpr uint32_t kStagingBytes = kEpiWarps * 32 * 128;  // 8 warps x (32 rows x 128 B)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSmemBytes = 1024 /*align slack*/ + kStages * kStageBytes + kStagingBytes + 256;
 
 __host__ __device__ constexpr int block_n_out(int epi) { return epi == kEpiSwiglu ? 128 : 256; }
 
-__device__ __forceinline__ void tile_coords(int tile, int m_blocks, int n_blocks, int& mb, int& nb) {
-  const int group_size = kGroupM * n_blocks;
+// Grouped raster: consecutive tiles walk `group` blocks of one axis (fast) while
+// sweeping the other, so concurrently running CTAs share operand tiles in L2.
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int tile, int& mb, int& nb) {
+  const int fast_blocks = p.raster_n ? p.n_blocks : p.m_blocks;
+  const int slow_blocks = p.raster_n ? p.m_blocks : p.n_blocks;
+  const int group_size = p.group * slow_blocks;
   const int g = tile / group_size;
-  const int first_m = g * kGroupM;
-  const int gm = min(kGroupM, m_blocks - first_m);
+  const int first = g * p.group;
+  const int gsz = min(p.group, fast_blocks - first);
   const int r = tile - g * group_size;
-  mb = first_m + r % gm;
-  nb = r / gm;
+  const int fast = first + r % gsz;
+  const int slow = r / gsz;
+  mb = p.raster_n ? slow : fast;
+  nb = p.raster_n ? fast : slow;
 }
 
 __device__ __forceinline__ float load_bias(const void* bias, int kind, int col, int n) {
@@ -116,7 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(bar_tfull + 8 * a, 1);
-      mbar_init(bar_tempty + 8 * a, 4);
+      mbar_init(bar_tempty + 8 * a, kEpiWarps);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -142,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
         int mb, nb;
-        tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
+        tile_coords(p, tile, mb, nb);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!wait_bounded(bar_empty + 8 * stage, phase ^ 1, abort_flag, p.status,
                             kStatusTimeoutProducer)) {
@@ -236,14 +247,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int ew = warp - 2;
-    const uint32_t stg0 = sStage + ew * (2 * 32 * 128);
+    const int quarter = warp & 3;        // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;    // which half of the tile's columns it converts
+    constexpr int kChunks = kBNOut / 64; // 64-column chunks per tile
+    constexpr int kMyChunks = kChunks / 2;
+    const uint32_t buf = sStage + (warp - 2) * (32 * 128);
     int local = 0;
-    int issued = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
       int mb, nb;
-      tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
+      tile_coords(p, tile, mb, nb);
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!wait_bounded(bar_tfull + 8 * acc, acc_phase, abort_flag, p.status,
@@ -254,9 +266,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row0 = mb * kBM + quarter * 32;
       const int col_base = nb * kBNOut;
 #pragma unroll 1
-      for (int c = 0; c < kBNOut / 64; ++c) {
-        const uint32_t buf = stg0 + (issued & 1) * (32 * 128);
-        if (lane == 0) bulk_wait_group_read<1>();
+      for (int cc = 0; cc < kMyChunks; ++cc) {
+        const int c = half * kMyChunks + cc;
+        // the previous store from this warp's staging buffer must have read it
+        if (lane == 0) bulk_wait_group_read<0>();
         __syncwarp();
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -276,15 +289,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else {
             uint32_t v[32];
             tmem_ld32(t_row + col0, v);
+            // one bias value per lane, broadcast across the row by shuffles
+            const float bl = load_bias(p.bias, p.bias_kind, col_base + col0 + lane, p.N_out);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              float x0 = __uint_as_float(v[2 * i]);
-              float x1 = __uint_as_float(v[2 * i + 1]);
-              if (p.bias_kind != kBiasNone) {
-                x0 += load_bias(p.bias, p.bias_kind, col_base + col0 + 2 * i, p.N_out);
-                x1 += load_bias(p.bias, p.bias_kind, col_base + col0 + 2 * i + 1, p.N_out);
-              }
+              float x0 = __uint_as_float(v[2 * i]) + __shfl_sync(0xffffffffu, bl, 2 * i);
+              float x1 = __uint_as_float(v[2 * i + 1]) + __shfl_sync(0xffffffffu, bl, 2 * i + 1);
               if constexpr (EPI == kEpiGelu) {
                 x0 = gelu_erf(x0);
                 x1 = gelu_erf(x1);
@@ -304,8 +315,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                          packed[4 * j + 3]);
           }
         }
-        if (c == kBNOut / 64 - 1) {
-          // All TMEM reads of this accumulator are done: hand it back to the MMA warp.
+        if (cc == kMyChunks - 1) {
+          // All TMEM reads of this warp for the accumulator are done: release it.
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
@@ -316,7 +327,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_store_2d(&tm_d, buf, col_base + c * 64, row0);
           bulk_commit_group();
         }
-        ++issued;
       }
     }
     if (lane == 0) bulk_wait_group<0>();

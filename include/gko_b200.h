@@ -155,6 +155,15 @@ int gko_fmha_varlen_fwd(int dtype, int64_t b, int64_t hq, int64_t hkv, int64_t d
 int gko_silu_mul(int dtype, int64_t n, const void* x, const void* y, void* out,
                  unsigned int* status, void* stream);
 
+/*
+ * Self-test of the failure path (no reference counterpart): launches one CTA
+ * that waits, through the operators' bounded wait, on a barrier nothing
+ * arrives on; after limit_ns (<= 2 s) it ORs GKO_STATUS_TIMEOUT_PRODUCER into
+ * *status and returns. Used by the tests to show that a stalled wait ends with
+ * a status bit instead of a hang.
+ */
+int gko_selftest_wait_timeout(unsigned int* status, long long limit_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
