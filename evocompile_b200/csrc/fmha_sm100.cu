@@ -44,11 +44,18 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
+// In tiles without masked keys, pair c of each 8 uses the FMA-pipe exponential when
+// bit (c % 8) is set, the MUFU otherwise (a knob for balancing the two pipes).
+#ifndef GKO_FMHA_POLY_PAIRS
+#define GKO_FMHA_POLY_PAIRS 0x00u  // measured fastest on B200: all exponentials on MUFU
+#endif
+constexpr uint32_t kPolyPairs = GKO_FMHA_POLY_PAIRS;
 
 struct Params {
   int hq, hkv, group;  // group = hq / hkv
   int sq, sk;          // dense: per-batch lengths; varlen: unused
-  int q_tiles;         // 256-row query blocks along the query axis (grid.y)
+  int q_tiles;         // 256-row query blocks along the query axis (grid.x)
+  int zh;              // batch (or sequences) x query heads
   float scale, scale_log2, softcap;
   int causal, window;
   // bias (dense only)
@@ -97,10 +104,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kIdescO = make_idesc_f16(kBF16, kBM, D, false, true);
 
   // ---------------------------------------------------------- block geometry
-  const int bh = blockIdx.x;
+  // grid.x walks the query blocks of one (batch, head) — heaviest (causal) first — so
+  // the CTAs running at the same time share that head's K/V in L2.
+  const int bh = (int)blockIdx.y + (int)blockIdx.z * (int)gridDim.y;
+  if (bh >= p.zh) return;
   const int h = bh % p.hq;
   const int zb = bh / p.hq;  // batch (dense) or sequence (varlen)
-  const int qb = p.q_tiles - 1 - (int)blockIdx.y;  // heaviest (causal) blocks first
+  const int qb = p.q_tiles - 1 - (int)blockIdx.x;
   const int m0 = qb * kBlockM;
   int len_q, len_k, row_q0, row_k0;
   if constexpr (VARLEN) {
@@ -158,11 +168,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bar_vfull = smeta + 40;    // [2]
   const uint32_t bar_vempty = smeta + 56;   // [2]
   const uint32_t bar_sfull = smeta + 72;    // [2] per query tile
-  const uint32_t bar_pfull = smeta + 88;    // [2] per query tile
-  const uint32_t bar_ofinal = smeta + 104;  // [2] per query tile
-  const uint32_t bar_drain = smeta + 120;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 128);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 132);
+  // [2 query tiles][2 halves]: P is handed over in two halves; a barrier per half
+  // completes once per key tile, so a waiter can never miss a phase.
+  const uint32_t bar_pfull = smeta + 88;
+  const uint32_t bar_ofinal = smeta + 120;  // [2] per query tile
+  const uint32_t bar_drain = smeta + 136;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 144);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 148);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -175,7 +187,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_vfull + 8 * i, 1);
       mbar_init(bar_vempty + 8 * i, 1);
       mbar_init(bar_sfull + 8 * i, 1);
-      mbar_init(bar_pfull + 8 * i, 4);
+      mbar_init(bar_pfull + 16 * i, 4);
+      mbar_init(bar_pfull + 16 * i + 8, 4);
       mbar_init(bar_ofinal + 8 * i, 1);
     }
     mbar_init(bar_drain, 1);
@@ -244,15 +257,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(bar_sfull + 8 * t);
       };
-      auto issue_pv = [&](int t, int u, bool first) {
+      // O_t += P_t V_j over keys [64 * half, 64 * half + 64) of the tile
+      auto issue_pv = [&](int t, int u, bool first, int half) {
         const int st = u & 1;
         const uint32_t v_addr = sb + L::kV0 + st * L::kTile;
         const uint32_t o_tmem = tmem_base + 256 + t * 128;
         const uint32_t p_tmem = tmem_base + t * kBN;
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
+        for (int k4 = 0; k4 < kBN / 32; ++k4) {
+          const int kk = half * (kBN / 32) + k4;
           mma_f16_ts(o_tmem, p_tmem + kk * 8, make_sdesc_sw128(v_addr + kk * 16 * 128, L::kChunk, 1024),
                      kIdescO, (!first || kk > 0) ? 1u : 0u);
+        }
       };
       // prologue: S_t for the first key tile
       if (ok) ok = wait_bounded(bar_kfull, 0, abort_flag, p.status, kStatusTimeoutMma);
@@ -276,10 +292,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int t = 0; t < kQTiles && ok; ++t) {
           if (j >= lo_t[t] && j < hi_t[t]) {
-            ok = wait_bounded(bar_pfull + 8 * t, (j - lo_t[t]) & 1, abort_flag, p.status, kStatusTimeoutMma);
+            // softmax hands P over in two halves, one barrier each
+#pragma unroll
+            for (int half = 0; half < 2 && ok; ++half) {
+              ok = wait_bounded(bar_pfull + 16 * t + 8 * half, (j - lo_t[t]) & 1, abort_flag, p.status,
+                                kStatusTimeoutMma);
+              if (!ok) break;
+              tc_fence_after();
+              issue_pv(t, u, j == lo_t[t], half);
+            }
             if (!ok) break;
-            tc_fence_after();
-            issue_pv(t, u, j == lo_t[t]);
             if (j == hi_t[t] - 1) mma_commit(bar_ofinal + 8 * t);
           }
           if (next && j + 1 >= lo_t[t] && j + 1 < hi_t[t]) issue_s(t, u + 1);
@@ -327,8 +349,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < kBN; ++c) s[c] = __uint_as_float(su[c]);
       }
-      // logits in the log2 domain
-      float tmax = -INFINITY;
+      // Row maximum. The plain path keeps raw scores (scale > 0 is folded into the
+      // exponent FFMA below); the general path converts to log2-domain logits first.
+      float kmul;  // multiplier taking s[] to the log2 domain
+      bool emulate = false;
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
       if constexpr (EXTRA) {
 #pragma unroll
         for (int c = 0; c < kBN; ++c) {
@@ -340,26 +365,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.causal) keep = keep && (kj <= qi);
           if (p.window > 0) keep = keep && (kj - qi <= p.window) && (qi - kj <= p.window);
           s[c] = keep ? x * kLog2e : -INFINITY;
-          tmax = fmaxf(tmax, s[c]);
         }
+        kmul = 1.f;
       } else {
         const bool need_mask = (kbase + kBN > len_k) || (p.causal && kbase + kBN - 1 > mt);
         if (need_mask) {
+          // keys kbase + c with c >= lim are masked (past the end, or after the query when causal)
+          const int lim = min(len_k, p.causal ? qi + 1 : len_k) - kbase;
 #pragma unroll
-          for (int c = 0; c < kBN; ++c) {
-            const int kj = kbase + c;
-            const bool keep = (kj < len_k) && (!p.causal || kj <= qi);
-            s[c] = keep ? s[c] * p.scale_log2 : -INFINITY;
-            tmax = fmaxf(tmax, s[c]);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < kBN; ++c) {
-            s[c] *= p.scale_log2;
-            tmax = fmaxf(tmax, s[c]);
-          }
+          for (int c = 0; c < kBN; ++c) s[c] = (c < lim) ? s[c] : -INFINITY;
         }
+        emulate = !need_mask;
+        kmul = p.scale_log2;
       }
+#pragma unroll
+      for (int c = 0; c < kBN; c += 8) {
+        mx0 = max3f(mx0, s[c], s[c + 1]);
+        mx1 = max3f(mx1, s[c + 2], s[c + 3]);
+        mx2 = max3f(mx2, s[c + 4], s[c + 5]);
+        mx3 = max3f(mx3, s[c + 6], s[c + 7]);
+      }
+      const float tmax = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * kmul;
       // lazy rescale: keep the old max unless the new one exceeds it by the threshold
       float m_new = m_run;
       float alpha = 1.f;
@@ -379,25 +405,51 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st32(o_tmem + c * 32, o);
         }
       }
-      // P_t (bf16/f16 pairs) into the first kBN/2 columns of the S_t region, 64 keys at a time
-      const float m_sub = (m_new == -INFINITY) ? 0.f : m_new;
-      float rsum = 0.f;
+      // P_t = 2^(kmul * s - m): one packed FFMA per pair, then MUFU.EX2 — or, in tiles
+      // without masked keys, the FMA-pipe polynomial for one pair in four. P (bf16/f16
+      // pairs) goes into the first kBN/2 columns of the S_t region, 64 keys at a time.
+      const float nm = (m_new == -INFINITY) ? 0.f : -m_new;
+      const uint64_t k2 = f2pack(kmul, kmul), nm2 = f2pack(nm, nm);
+      float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+      auto exp_row = [&](auto poly_tag) {
+        constexpr bool kPoly = decltype(poly_tag)::value;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pk[32];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float p0 = fast_exp2(s[half * 64 + 2 * c] - m_sub);
-          const float p1 = fast_exp2(s[half * 64 + 2 * c + 1] - m_sub);
-          rsum += p0 + p1;
-          pk[c] = Cvt<T>::pack(p0, p1);
+          for (int c = 0; c < 32; ++c) {
+            uint64_t x = fma2(f2pack(s[half * 64 + 2 * c], s[half * 64 + 2 * c + 1]), k2, nm2);
+            if (kPoly && ((kPolyPairs >> (c & 7)) & 1)) {
+              x = exp2_poly_x2(x);
+            } else {
+              float a, b;
+              f2unpack(x, a, b);
+              x = f2pack(fast_exp2(a), fast_exp2(b));
+            }
+            float a, b;
+            f2unpack(x, a, b);
+            if (c & 1) {
+              acc2 += a;
+              acc3 += b;
+            } else {
+              acc0 += a;
+              acc1 += b;
+            }
+            pk[c] = Cvt<T>::pack(a, b);
+          }
+          tmem_st32(s_tmem + half * 32, pk);
+          // hand this half of P to the MMA warp
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_pfull + 16 * t + 8 * half);
         }
-        tmem_st32(s_tmem + half * 32, pk);
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_pfull + 8 * t);
+      };
+      if (kPolyPairs != 0 && emulate)
+        exp_row(std::true_type{});
+      else
+        exp_row(std::false_type{});
+      const float rsum = (acc0 + acc1) + (acc2 + acc3);
       l_run = l_run * alpha + rsum;
       m_run = m_new;
     }
@@ -479,6 +531,12 @@ int dispatch(int d, bool extra, const CUtensorMap& tq, const CUtensorMap& tk, co
                  : launch<T, 64, VARLEN, false>(tq, tk, tv, p, grid, s);
   return extra ? launch<T, 128, VARLEN, true>(tq, tk, tv, p, grid, s)
                : launch<T, 128, VARLEN, false>(tq, tk, tv, p, grid, s);
+}
+
+// Grid: query blocks along x, (batch, head) pairs along y (and z beyond 65535).
+dim3 grid_of(int q_blocks, int zh) {
+  const unsigned y = (unsigned)(zh < 65535 ? zh : 65535);
+  return dim3((unsigned)q_blocks, y, (unsigned)((zh + (int)y - 1) / (int)y));
 }
 
 // 4-D tensor map over (d, s, h, z) for one operand; strides in elements for (z, h, s).
@@ -584,8 +642,8 @@ extern "C" int gko_fmha_fwd(int dtype, int64_t z, int64_t hq, int64_t hkv, int64
   p.lse_stride_h = sq;
   p.status = status;
   const bool extra = bias_mode != GKO_BIAS_NONE || softcap > 0.f || window > 0;
-  dim3 grid((unsigned)(z * hq), (unsigned)p.q_tiles);
-  if (grid.y > 65535) return fail(GKO_ERR_UNSUPPORTED, "fmha supports sq <= 8388480");
+  p.zh = (int)(z * hq);
+  const dim3 grid = fmha::grid_of(p.q_tiles, p.zh);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == GKO_BF16) return fmha::dispatch<__nv_bfloat16, false>((int)d, extra, tq, tk, tv, p, grid, s);
   return fmha::dispatch<__half, false>((int)d, extra, tq, tk, tv, p, grid, s);
@@ -634,8 +692,8 @@ extern "C" int gko_fmha_varlen_fwd(int dtype, int64_t b, int64_t hq, int64_t hkv
   p.total_q = (int)tq;
   p.status = status;
   const bool extra = softcap > 0.f || window > 0;
-  dim3 grid((unsigned)(b * hq), (unsigned)p.q_tiles);
-  if (grid.y > 65535) return fail(GKO_ERR_UNSUPPORTED, "fmha supports max_seqlen_q <= 8388480");
+  p.zh = (int)(b * hq);
+  const dim3 grid = fmha::grid_of(p.q_tiles, p.zh);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (dtype == GKO_BF16) return fmha::dispatch<__nv_bfloat16, true>((int)d, extra, mq, mk, mv, p, grid, s);
   return fmha::dispatch<__half, true>((int)d, extra, mq, mk, mv, p, grid, s);
