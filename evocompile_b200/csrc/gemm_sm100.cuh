@@ -91,6 +91,81 @@ __device__ __forceinline__ float gelu_erf(float x) {
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
 
+// Converts this warp's half of one accumulator tile (32 TMEM lanes starting at
+// t_row) into the output: TMEM -> registers -> epilogue math -> 128B-swizzled
+// staging buffer -> TMA store of [32 rows x 64 columns] per chunk. Calls
+// `release()` (on one lane, after the warp's last TMEM read of the tile) so the
+// MMA warp may reuse the accumulator.
+template <typename T, int EPI, typename Release>
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtensorMap* tm_d,
+                                              uint32_t t_row, int row0, int col_base, int half,
+                                              uint32_t buf, int lane, Release release) {
+  constexpr int kBNOut = block_n_out(EPI);
+  constexpr int kChunks = kBNOut / 64;
+  constexpr int kMyChunks = kChunks / 2;
+#pragma unroll 1
+  for (int cc = 0; cc < kMyChunks; ++cc) {
+    const int c = half * kMyChunks + cc;
+    // the previous store from this warp's staging buffer must have read it
+    if (lane == 0) bulk_wait_group_read<0>();
+    __syncwarp();
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int col0 = c * 64 + h * 32;
+      uint32_t packed[16];
+      if constexpr (EPI == kEpiSwiglu) {
+        uint32_t g[32], u[32];
+        tmem_ld32(t_row + col0, g);
+        tmem_ld32(t_row + 128 + col0, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
+          const float u0 = __uint_as_float(u[2 * i]), u1 = __uint_as_float(u[2 * i + 1]);
+          packed[i] = Cvt<T>::pack(silu(g0) * u0, silu(g1) * u1);
+        }
+      } else {
+        uint32_t v[32];
+        tmem_ld32(t_row + col0, v);
+        // one bias value per lane, broadcast across the row by shuffles
+        const float bl = load_bias(p.bias, p.bias_kind, col_base + col0 + lane, p.N_out);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float x0 = __uint_as_float(v[2 * i]) + __shfl_sync(0xffffffffu, bl, 2 * i);
+          float x1 = __uint_as_float(v[2 * i + 1]) + __shfl_sync(0xffffffffu, bl, 2 * i + 1);
+          if constexpr (EPI == kEpiGelu) {
+            x0 = gelu_erf(x0);
+            x1 = gelu_erf(x1);
+          } else if constexpr (EPI == kEpiRelu) {
+            x0 = fmaxf(x0, 0.f);
+            x1 = fmaxf(x1, 0.f);
+          }
+          packed[i] = Cvt<T>::pack(x0, x1);
+        }
+      }
+      // 128B-swizzled staging row: 16-byte piece j of row `lane` lives at j ^ (lane & 7).
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int piece = h * 4 + j;
+        const uint32_t addr = buf + lane * 128 + ((piece ^ (lane & 7)) << 4);
+        st_shared_v4(addr, packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+      }
+    }
+    if (cc == kMyChunks - 1) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) release();
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d_hint(tm_d, buf, col_base + c * 64, row0, l2_policy_evict_first());
+      bulk_commit_group();
+    }
+  }
+}
+
 template <typename T, int EPI, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
@@ -151,6 +226,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // the operand a raster group shares stays in L2; the streamed one goes first
+      const uint64_t keep = l2_policy_evict_last(), stream = l2_policy_evict_first();
+      const uint64_t pol_a = p.raster_n ? stream : keep, pol_b = p.raster_n ? keep : stream;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
         int mb, nb;
         tile_coords(p, tile, mb, nb);
@@ -165,15 +243,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a_dst = sA + stage * kABytes;
           const uint32_t b_dst = sB + stage * kBBytes;
           const int k0 = kb * kBK;
-          tma_load_2d(a_dst, &tm_a, full, k0, mb * kBM);
+          tma_load_2d_hint(a_dst, &tm_a, full, k0, mb * kBM, pol_a);
           if constexpr (!B_MN) {
             // B is [N, K] K-major: two 128-row boxes.
             if constexpr (EPI == kEpiSwiglu) {
-              tma_load_2d(b_dst, &tm_b, full, k0, nb * 128);
-              tma_load_2d(b_dst + kBBytes / 2, &tm_b, full, k0, p.up_offset + nb * 128);
+              tma_load_2d_hint(b_dst, &tm_b, full, k0, nb * 128, pol_b);
+              tma_load_2d_hint(b_dst + kBBytes / 2, &tm_b, full, k0, p.up_offset + nb * 128, pol_b);
             } else {
-              tma_load_2d(b_dst, &tm_b, full, k0, nb * 256);
-              tma_load_2d(b_dst + kBBytes / 2, &tm_b, full, k0, nb * 256 + 128);
+              tma_load_2d_hint(b_dst, &tm_b, full, k0, nb * 256, pol_b);
+              tma_load_2d_hint(b_dst + kBBytes / 2, &tm_b, full, k0, nb * 256 + 128, pol_b);
             }
           } else {
             // B is [K, N] MN-major: four 64-column boxes, 64 K-rows each.
@@ -184,7 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 col = (c < 2) ? nb * 128 + c * 64 : p.up_offset + nb * 128 + (c - 2) * 64;
               else
                 col = nb * 256 + c * 64;
-              tma_load_2d(b_dst + c * (kBBytes / 4), &tm_b, full, col, k0);
+              tma_load_2d_hint(b_dst + c * (kBBytes / 4), &tm_b, full, col, k0, pol_b);
             }
           }
           if (++stage == kStages) {
@@ -249,8 +327,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;        // TMEM lane quarter this warp may access
     const int half = (warp - 2) >> 2;    // which half of the tile's columns it converts
-    constexpr int kChunks = kBNOut / 64; // 64-column chunks per tile
-    constexpr int kMyChunks = kChunks / 2;
     const uint32_t buf = sStage + (warp - 2) * (32 * 128);
     int local = 0;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
@@ -265,69 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t_row = tmem_base + acc * kMmaN + (static_cast<uint32_t>(quarter * 32) << 16);
       const int row0 = mb * kBM + quarter * 32;
       const int col_base = nb * kBNOut;
-#pragma unroll 1
-      for (int cc = 0; cc < kMyChunks; ++cc) {
-        const int c = half * kMyChunks + cc;
-        // the previous store from this warp's staging buffer must have read it
-        if (lane == 0) bulk_wait_group_read<0>();
-        __syncwarp();
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int col0 = c * 64 + h * 32;
-          uint32_t packed[16];
-          if constexpr (EPI == kEpiSwiglu) {
-            uint32_t g[32], u[32];
-            tmem_ld32(t_row + col0, g);
-            tmem_ld32(t_row + 128 + col0, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
-              const float u0 = __uint_as_float(u[2 * i]), u1 = __uint_as_float(u[2 * i + 1]);
-              packed[i] = Cvt<T>::pack(silu(g0) * u0, silu(g1) * u1);
-            }
-          } else {
-            uint32_t v[32];
-            tmem_ld32(t_row + col0, v);
-            // one bias value per lane, broadcast across the row by shuffles
-            const float bl = load_bias(p.bias, p.bias_kind, col_base + col0 + lane, p.N_out);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              float x0 = __uint_as_float(v[2 * i]) + __shfl_sync(0xffffffffu, bl, 2 * i);
-              float x1 = __uint_as_float(v[2 * i + 1]) + __shfl_sync(0xffffffffu, bl, 2 * i + 1);
-              if constexpr (EPI == kEpiGelu) {
-                x0 = gelu_erf(x0);
-                x1 = gelu_erf(x1);
-              } else if constexpr (EPI == kEpiRelu) {
-                x0 = fmaxf(x0, 0.f);
-                x1 = fmaxf(x1, 0.f);
-              }
-              packed[i] = Cvt<T>::pack(x0, x1);
-            }
-          }
-          // 128B-swizzled staging row: 16-byte piece j of row `lane` lives at j ^ (lane & 7).
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int piece = h * 4 + j;
-            const uint32_t addr = buf + lane * 128 + ((piece ^ (lane & 7)) << 4);
-            st_shared_v4(addr, packed[4 * j], packed[4 * j + 1], packed[4 * j + 2],
-                         packed[4 * j + 3]);
-          }
-        }
-        if (cc == kMyChunks - 1) {
-          // All TMEM reads of this warp for the accumulator are done: release it.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tm_d, buf, col_base + c * 64, row0);
-          bulk_commit_group();
-        }
-      }
+      epilogue_tile<T, EPI>(p, &tm_d, t_row, row0, col_base, half, buf, lane,
+                            [&] { mbar_arrive(bar_tempty + 8 * acc); });
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
@@ -338,6 +353,214 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, kTmemCols);
+}
+
+
+// ---------------------------------------------------------------------------
+// CTA-pair version (cta_group::2): a cluster of two CTAs on neighbouring SMs
+// computes a 256 x 256 accumulator tile. CTA r of the pair loads rows
+// [128 r, 128 r + 128) of the A tile and columns [128 r, 128 r + 128) of the
+// B tile (SwiGLU: CTA 0 the gate columns, CTA 1 the up columns) into its own
+// shared memory; the leader (r = 0) issues M = 256 MMAs that read both CTAs'
+// operands and write each CTA's 128 accumulator rows into that CTA's TMEM. Each
+// SM therefore streams half of B per MMA: 64 instead of 96 bytes of shared
+// memory per tensor-core cycle, and a third less L2 traffic.
+//   full[s]   (leader only)  both CTAs' TMA bytes for stage s; leader's producer arrives
+//   empty[s]  (both)         leader's MMA commit to each CTA when stage s is consumed
+//   tfull[a]  (both)         leader's MMA commit to each CTA when accumulator a is done
+//   tempty[a] (leader only)  16 epilogue warps (8 per CTA) release accumulator a
+// No TMA multicast: every CTA loads its own operands.
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairStageBytes = 2 * 128 * kBK * 2;  // A half + B half: 32 KB
+constexpr uint32_t kPairSmemBytes = 1024 + kPairStages * kPairStageBytes + kStagingBytes + 256;
+
+template <typename T, int EPI, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                     const __grid_constant__ CUtensorMap tm_d, const GemmParams p) {
+  constexpr int kBNOut = block_n_out(EPI);
+  constexpr uint32_t kIdesc =
+      make_idesc_f16(std::is_same<T, __nv_bfloat16>::value, 2 * kBM, kMmaN, false, B_MN);
+  constexpr uint32_t kHalfBytes = 128 * kBK * 2;  // 16 KB
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  const uint32_t sbase = raw_addr + pad;
+  const uint32_t sA = sbase;                               // [stages][128 x 64]
+  const uint32_t sB = sA + kPairStages * kHalfBytes;      // [stages][128 x 64]
+  const uint32_t sStage = sB + kPairStages * kHalfBytes;
+  uint8_t* meta = smem + kPairStages * kPairStageBytes + kStagingBytes;
+  const uint32_t smeta = sStage + kStagingBytes;
+  const uint32_t bar_full = smeta;                      // [6]
+  const uint32_t bar_empty = smeta + 8 * kPairStages;   // [6]
+  const uint32_t bar_tfull = smeta + 16 * kPairStages;  // [2]
+  const uint32_t bar_tempty = bar_tfull + 16;           // [2]
+  const uint32_t bar_drain = bar_tempty + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 16 * kPairStages + 40);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 16 * kPairStages + 48);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1;
+  const int clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kPairStages; ++st) {
+      mbar_init(bar_full + 8 * st, 1);
+      mbar_init(bar_empty + 8 * st, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar_tfull + 8 * a, 1);
+      mbar_init(bar_tempty + 8 * a, 2 * kEpiWarps);
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tm_a);
+    prefetch_tmap(&tm_b);
+    prefetch_tmap(&tm_d);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      const uint64_t keep = l2_policy_evict_last(), stream = l2_policy_evict_first();
+      const uint64_t pol_a = p.raster_n ? stream : keep, pol_b = p.raster_n ? keep : stream;
+      for (int tile = cluster; tile < p.num_tiles && ok; tile += clusters) {
+        int mb, nb;
+        tile_coords(p, tile, mb, nb);
+        const int row_a = mb * 2 * kBM + (int)rank * kBM;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bounded_cluster(bar_empty + 8 * stage, phase ^ 1, abort_flag, p.status,
+                                    kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_local = bar_full + 8 * stage;
+          const uint32_t full_leader = mapa_shared(full_local, 0);
+          if (leader) mbar_arrive_expect_tx(full_local, 2 * kPairStageBytes);
+          const int k0 = kb * kBK;
+          tma_load_2d_pair_hint(sA + stage * kHalfBytes, &tm_a, full_leader, k0, row_a, pol_a);
+          const uint32_t b_dst = sB + stage * kHalfBytes;
+          if constexpr (!B_MN) {
+            int brow;
+            if constexpr (EPI == kEpiSwiglu)
+              brow = rank ? p.up_offset + nb * 128 : nb * 128;
+            else
+              brow = nb * 256 + (int)rank * 128;
+            tma_load_2d_pair_hint(b_dst, &tm_b, full_leader, k0, brow, pol_b);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              int col;
+              if constexpr (EPI == kEpiSwiglu)
+                col = (rank ? p.up_offset : 0) + nb * 128 + c * 64;
+              else
+                col = nb * 256 + (int)rank * 128 + c * 64;
+              tma_load_2d_pair_hint(b_dst + c * (kHalfBytes / 2), &tm_b, full_leader, col, k0, pol_b);
+            }
+          }
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (lane == 0 && leader) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = cluster; tile < p.num_tiles && ok; tile += clusters, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!wait_bounded_cluster(bar_tempty + 8 * acc, acc_phase ^ 1, abort_flag, p.status, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kMmaN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bounded(bar_full + 8 * stage, phase, abort_flag, p.status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = sA + stage * kHalfBytes;
+          const uint32_t b_addr = sB + stage * kHalfBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t adesc = make_sdesc_sw128(a_addr + kk * 32, 16, 1024);
+            uint64_t bdesc;
+            if constexpr (!B_MN)
+              bdesc = make_sdesc_sw128(b_addr + kk * 32, 16, 1024);
+            else
+              bdesc = make_sdesc_sw128(b_addr + kk * 16 * 128, kHalfBytes / 2, 1024);
+            mma_f16_ss_pair(d_tmem, adesc, bdesc, kIdesc, (kb | kk) != 0);
+          }
+          // release stage `stage` in both CTAs once these MMAs have read it
+          mma_commit_pair(bar_empty + 8 * stage);
+          mma_commit_pair(mapa_shared(bar_empty + 8 * stage, 1));
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(bar_tfull + 8 * acc);
+        mma_commit_pair(mapa_shared(bar_tfull + 8 * acc, 1));
+      }
+      if (*abort_flag) {
+        mma_commit_pair(bar_drain);
+        wait_for(bar_drain, 0, p.status, kStatusTimeoutDrain);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t buf = sStage + (warp - 2) * (32 * 128);
+    int local = 0;
+    for (int tile = cluster; tile < p.num_tiles; tile += clusters, ++local) {
+      int mb, nb;
+      tile_coords(p, tile, mb, nb);
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!wait_bounded_cluster(bar_tfull + 8 * acc, acc_phase, abort_flag, p.status, kStatusTimeoutEpilogue))
+        break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + acc * kMmaN + (static_cast<uint32_t>(quarter * 32) << 16);
+      const int row0 = mb * 2 * kBM + (int)rank * kBM + quarter * 32;
+      const uint32_t tempty_leader = mapa_shared(bar_tempty + 8 * acc, 0);
+      epilogue_tile<T, EPI>(p, &tm_d, t_row, row0, nb * kBNOut, half, buf, lane,
+                            [&] { mbar_arrive_cluster(tempty_leader); });
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // all MMAs done and all cross-CTA signals delivered before teardown
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, kTmemCols);
 }
 
 }  // namespace gemm
