@@ -46,7 +46,7 @@ SIGNATURES = {
     "gko_fmha_fwd": (
         _int,
         [_int, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _p64, _vp, _p64, _vp, _p64, _vp, _int, _int,
-         _p64, _i64, _fl, _int, _int, _fl, _vp, _vp, _vp, _vp],
+         _p64, _i64, _p64, _fl, _int, _int, _fl, _vp, _vp, _vp, _vp],
     ),
     "gko_fmha_varlen_fwd": (
         _int,
@@ -55,6 +55,8 @@ SIGNATURES = {
     ),
     "gko_silu_mul": (_int, [_int, _i64, _vp, _vp, _vp, _vp, _vp]),
     "gko_selftest_wait_timeout": (_int, [_vp, ctypes.c_longlong, _vp]),
+    "gko_rmsnorm": (_int, [_int, _i64, _i64, _vp, _vp, _vp, _fl, _vp, _vp, _i64, _vp, _vp]),
+    "gko_rope": (_int, [_int, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _fl, _vp, _vp]),
 }
 
 

@@ -1,0 +1,140 @@
+"""Llama-3-70B-shaped transformer block (prefill) on the fused operators, tensor-parallel.
+
+    x -> RMSNorm -> QKV GEMM -> RoPE(q, k) -> causal GQA attention -> o-proj -> all-reduce
+      -> + x -> RMSNorm -> gate/up GEMM + SwiGLU -> down GEMM -> all-reduce -> + residual
+
+Megatron-style split over ``world`` ranks (one process per GPU): the QKV projection is
+column-parallel by kv group (each rank owns Hkv/world kv heads and the Hq/world query heads
+that use them), the o-projection row-parallel; gate/up column-parallel (each rank owns
+d_ff/world gate rows and the matching up rows), the down projection row-parallel. The two
+row-parallel outputs are summed with an NCCL all-reduce. RMSNorm weights are replicated.
+
+Every GEMM is the tcgen05 kernel (the SwiGLU one fused), attention the tcgen05 FMHA reading
+q/k/v in place from the QKV output and writing [tokens, heads, d] for the o-projection,
+RMSNorm (+ residual add) and RoPE are the library's memory-bound kernels.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+
+
+@dataclass(frozen=True)
+class BlockConfig:
+    d_model: int = 8192
+    n_heads: int = 64
+    n_kv_heads: int = 8
+    head_dim: int = 128
+    d_ff: int = 28672
+    eps: float = 1e-5
+    rope_theta: float = 500000.0
+
+    def flops(self, tokens: int, seq_len: int) -> float:
+        """Algorithmic FLOP of one block forward over `tokens` tokens in sequences of `seq_len` (causal)."""
+        d, hd = self.d_model, self.head_dim
+        qkv = 2.0 * tokens * d * (self.n_heads + 2 * self.n_kv_heads) * hd
+        attn = 2.0 * self.n_heads * hd * seq_len * seq_len * (tokens / seq_len)  # causal half of 4·H·S²·D per seq
+        oproj = 2.0 * tokens * self.n_heads * hd * d
+        gateup = 2.0 * tokens * d * 2 * self.d_ff
+        down = 2.0 * tokens * self.d_ff * d
+        return qkv + attn + oproj + gateup + down
+
+
+WEIGHT_NAMES = ("attn_norm", "wq", "wk", "wv", "wo", "mlp_norm", "w_gate", "w_up", "w_down")
+
+
+def init_weights(cfg: BlockConfig, device, dtype=torch.bfloat16, seed: int = 0, std: float = 0.02):
+    """Full (unsharded) random-init weights: projections ~ N(0, std), norm weights 1."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    d, hd = cfg.d_model, cfg.head_dim
+
+    def w(rows, cols):
+        return (torch.randn(rows, cols, device=device, generator=g) * std).to(dtype)
+
+    return {
+        "attn_norm": torch.ones(d, device=device, dtype=dtype),
+        "wq": w(cfg.n_heads * hd, d),
+        "wk": w(cfg.n_kv_heads * hd, d),
+        "wv": w(cfg.n_kv_heads * hd, d),
+        "wo": w(d, cfg.n_heads * hd),
+        "mlp_norm": torch.ones(d, device=device, dtype=dtype),
+        "w_gate": w(cfg.d_ff, d),
+        "w_up": w(cfg.d_ff, d),
+        "w_down": w(d, cfg.d_ff),
+    }
+
+
+def shard_weights(full: dict, cfg: BlockConfig, rank: int, world: int) -> dict:
+    """This rank's slice of the block weights (column-parallel QKV and gate/up, row-parallel o/down).
+
+    Returns wqkv [(hq_l + 2 hkv_l) * D, d] (rows: local q heads, then local k heads, then local v heads),
+    wo [d, hq_l * D], w_gate_up [2 * ff_l, d] (local gate rows then local up rows), w_down [d, ff_l],
+    and the replicated norm weights.
+    """
+    if cfg.n_kv_heads % world or cfg.n_heads % world or cfg.d_ff % world:
+        raise ValueError(f"world {world} must divide kv heads {cfg.n_kv_heads}, heads and d_ff")
+    hd = cfg.head_dim
+    hkv_l = cfg.n_kv_heads // world
+    hq_l = cfg.n_heads // world
+    ff_l = cfg.d_ff // world
+    q_rows = slice(rank * hq_l * hd, (rank + 1) * hq_l * hd)
+    kv_rows = slice(rank * hkv_l * hd, (rank + 1) * hkv_l * hd)
+    ff = slice(rank * ff_l, (rank + 1) * ff_l)
+    return {
+        "attn_norm": full["attn_norm"],
+        "mlp_norm": full["mlp_norm"],
+        "wqkv": torch.cat([full["wq"][q_rows], full["wk"][kv_rows], full["wv"][kv_rows]], 0).contiguous(),
+        "wo": full["wo"][:, q_rows].contiguous(),
+        "w_gate_up": torch.cat([full["w_gate"][ff], full["w_up"][ff]], 0).contiguous(),
+        "w_down": full["w_down"][:, ff].contiguous(),
+        "hq_local": hq_l,
+        "hkv_local": hkv_l,
+    }
+
+
+class TPBlock:
+    """One rank of the tensor-parallel block. ``group`` is a torch.distributed process group
+    (NCCL) or None for a single GPU."""
+
+    def __init__(self, local: dict, cfg: BlockConfig, group=None):
+        self.w = local
+        self.cfg = cfg
+        self.group = group
+        self.world = 1 if group is None else torch.distributed.get_world_size(group)
+
+    def _all_reduce(self, t):
+        if self.world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM, group=self.group)
+        return t
+
+    def forward(self, x: torch.Tensor, events=None) -> torch.Tensor:
+        """x [B, S, d_model] (bf16) -> [B, S, d_model]. ``events`` (start, end) CUDA events, if
+        given, bracket the fused gate/up kernel (for per-kernel timing)."""
+        cfg, w = self.cfg, self.w
+        B, S, d = x.shape
+        T, hd = B * S, cfg.head_dim
+        hq, hkv = w["hq_local"], w["hkv_local"]
+        x2 = x.reshape(T, d)
+        h = ops.rmsnorm(x2, w["attn_norm"], cfg.eps)
+        qkv = ops.linear(h, w["wqkv"])                                    # [T, (hq + 2 hkv) * D]
+        q = qkv[:, : hq * hd].view(T, hq, hd)
+        k = qkv[:, hq * hd: (hq + hkv) * hd].view(T, hkv, hd)
+        v = qkv[:, (hq + hkv) * hd:].view(T, hkv, hd)
+        ops.rope_(q, cfg.rope_theta, seq_len=S)
+        ops.rope_(k, cfg.rope_theta, seq_len=S)
+        as4 = lambda t: t.view(B, S, t.shape[1], hd).transpose(1, 2)     # noqa: E731  [B, H, S, D] views
+        attn = torch.empty(T, hq, hd, device=x.device, dtype=x.dtype)
+        ops.fmha_fwd(as4(q), as4(k), as4(v), None, hd ** -0.5, 1, out=as4(attn))
+        o = self._all_reduce(ops.linear(attn.view(T, hq * hd), w["wo"]))  # row-parallel partial -> sum
+        h2, x1 = ops.rmsnorm(o, w["mlp_norm"], cfg.eps, residual=x2, return_sum=True)
+        if events is not None:
+            events[0].record()
+        g = ops.linear_swiglu(h2, w["w_gate_up"])                        # [T, ff_local]
+        if events is not None:
+            events[1].record()
+        dn = self._all_reduce(ops.linear(g, w["w_down"]))
+        return (x1 + dn).view(B, S, d)

@@ -64,6 +64,7 @@ struct Params {
   int64_t b_sz, b_sh, b_sq, b_sk;
   // outputs
   void* out;
+  int64_t o_sz, o_sh, o_ss;  // dense output element strides (z, h, s); d stride 1
   float* lse;
   int64_t lse_stride_h;  // dense: sq (rows of one head); varlen: total tokens
   const int* cu_q;
@@ -465,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (VARLEN)
       orow = reinterpret_cast<T*>(p.out) + ((int64_t)(row_q0 + qi) * p.hq + h) * D;
     else
-      orow = reinterpret_cast<T*>(p.out) + (((int64_t)zb * p.hq + h) * p.sq + qi) * D;
+      orow = reinterpret_cast<T*>(p.out) + (int64_t)zb * p.o_sz + (int64_t)h * p.o_sh + (int64_t)qi * p.o_ss;
     const float inv = (l_run > 0.f) ? 1.f / l_run : 0.f;
     if (ok && has) {
 #pragma unroll
@@ -573,7 +574,7 @@ extern "C" int gko_fmha_fwd(int dtype, int64_t z, int64_t hq, int64_t hkv, int64
                             int64_t d, const void* q, const int64_t* qs, const void* k,
                             const int64_t* ks, const void* v, const int64_t* vs, const void* bias,
                             int bias_mode, int bias_dtype, const int64_t* bs, int64_t bias_batch,
-                            float scale,
+                            const int64_t* os, float scale,
                             int causal, int window, float softcap, void* out, float* lse,
                             unsigned int* status, void* stream) {
   int rc = fmha::check_common(dtype, hq, hkv, d, scale, window, softcap);
@@ -638,6 +639,17 @@ extern "C" int gko_fmha_fwd(int dtype, int64_t z, int64_t hq, int64_t hkv, int64
     p.bias_z = (int)bias_batch;
   }
   p.out = out;
+  if (os) {
+    if (os[3] != 1 || os[0] % 8 || os[1] % 8 || os[2] % 8 || os[0] < 0 || os[1] < 0 || os[2] < 0)
+      return fail(GKO_ERR_UNSUPPORTED, "fmha output needs unit d stride and other strides multiples of 8");
+    p.o_sz = os[0];
+    p.o_sh = os[1];
+    p.o_ss = os[2];
+  } else {
+    p.o_ss = d;
+    p.o_sh = sq * d;
+    p.o_sz = hq * sq * d;
+  }
   p.lse = lse;
   p.lse_stride_h = sq;
   p.status = status;

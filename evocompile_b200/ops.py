@@ -151,6 +151,50 @@ def silu_mul(x, y):
     return out
 
 
+def rmsnorm(x, weight, eps=1e-5, residual=None, return_sum=False):
+    """rmsnorm(x (+ residual)) * weight over the last dim; with return_sum also x + residual."""
+    dev = _lib.require_cuda(x, weight, residual)
+    cols = x.shape[-1]
+    x2 = x.reshape(-1, cols).contiguous()
+    r2 = residual.reshape(-1, cols).contiguous() if residual is not None else None
+    out = torch.empty(x2.shape, device=dev, dtype=x.dtype)
+    total = torch.empty(x2.shape, device=dev, dtype=x.dtype) if (return_sum and r2 is not None) else None
+    w = weight.contiguous()
+    if x2.shape[0]:
+        with torch.cuda.device(dev):
+            rc = _lib.load().gko_rmsnorm(
+                _lib.dtype_code(x.dtype), x2.shape[0], cols, _ptr(x2), _ptr(r2), _ptr(w), float(eps), _ptr(out),
+                _ptr(total), cols, _status_ptr(dev), _stream(dev),
+            )
+        _lib.check(rc, "gko_rmsnorm")
+    out = out.reshape(x.shape)
+    if return_sum:
+        return out, (total.reshape(x.shape) if total is not None else x)
+    return out
+
+
+def rope_(x, theta=500000.0, positions=None, seq_len=None):
+    """Rotate-half RoPE in place on x [tokens, heads, head_dim] (any token/head strides, unit dim stride).
+
+    Position of token t: positions[t] (int32 tensor) or t % seq_len.
+    """
+    dev = _lib.require_cuda(x, positions)
+    if x.dim() != 3 or x.stride(-1) != 1:
+        raise RuntimeError("rope_: x must be [tokens, heads, head_dim] with unit stride along head_dim")
+    t, h, d = x.shape
+    pos = positions.to(torch.int32).contiguous() if positions is not None else None
+    if pos is None and not seq_len:
+        seq_len = t
+    if t and h:
+        with torch.cuda.device(dev):
+            rc = _lib.load().gko_rope(
+                _lib.dtype_code(x.dtype), t, h, d, _ptr(x), x.stride(0), x.stride(1), _ptr(pos),
+                int(seq_len or 0), float(theta), _status_ptr(dev), _stream(dev),
+            )
+        _lib.check(rc, "gko_rope")
+    return x
+
+
 # --------------------------------------------------------------------------- attention
 def _bias_layout(q, k, attn_bias):
     """Map an additive attention bias onto the kernel's bias modes.
@@ -200,8 +244,11 @@ def _bias_layout(q, k, attn_bias):
     )
 
 
-def fmha_fwd(q, k, v, attn_bias=None, scale=None, causal=0, window=0, softcap=0.0):
-    """Fused attention forward -> (out [z, hq, sq, d] contiguous, lse f32 [z * hq, sq]).
+def fmha_fwd(q, k, v, attn_bias=None, scale=None, causal=0, window=0, softcap=0.0, out=None):
+    """Fused attention forward -> (out [z, hq, sq, d], lse f32 [z * hq, sq]).
+
+    ``out`` (optional) is a preallocated output with any strides allowed by the kernel (e.g. a
+    [z, s, h, d] buffer viewed as [z, h, s, d]); by default a fresh contiguous tensor.
 
     q [z, hq, sq, d], k/v [z, hkv, sk, d] with hq % hkv == 0 (GQA); any
     strides with unit stride along d (e.g. [z, s, h, d] storage viewed through
@@ -228,7 +275,10 @@ def fmha_fwd(q, k, v, attn_bias=None, scale=None, causal=0, window=0, softcap=0.
 
     q, k, v = _fix(q), _fix(k), _fix(v)
     bias_t, mode, bstr, nb = _bias_layout(q, k, attn_bias)
-    out = torch.empty((z, hq, sq, d), device=dev, dtype=q.dtype)
+    if out is None:
+        out = torch.empty((z, hq, sq, d), device=dev, dtype=q.dtype)
+    elif out.shape != (z, hq, sq, d) or out.dtype != q.dtype or out.device != dev:
+        raise RuntimeError(f"fmha: out must be [{z}, {hq}, {sq}, {d}] {q.dtype} on {dev}")
     lse = torch.empty((z * hq, sq), device=dev, dtype=torch.float32)
     if z and hq and sq:
         with torch.cuda.device(dev):
@@ -236,7 +286,8 @@ def fmha_fwd(q, k, v, attn_bias=None, scale=None, causal=0, window=0, softcap=0.
                 dt, z, hq, hkv, sq, sk, d,
                 _ptr(q), _I64x4(*q.stride()), _ptr(k), _I64x4(*k.stride()), _ptr(v), _I64x4(*v.stride()),
                 _ptr(bias_t), mode, _lib.dtype_code(bias_t.dtype) if bias_t is not None else 0,
-                _I64x4(*bstr), nb, float(scale), int(bool(causal)), int(window or 0), float(softcap or 0.0),
+                _I64x4(*bstr), nb, _I64x4(*out.stride()), float(scale), int(bool(causal)), int(window or 0),
+                float(softcap or 0.0),
                 _ptr(out), _ptr(lse), _status_ptr(dev), _stream(dev),
             )
         _lib.check(rc, "gko_fmha_fwd")

@@ -117,15 +117,18 @@ int gko_linear_swiglu(int dtype, int64_t m, int64_t h, int64_t k, const void* x,
  * |key - query| <= window; softcap > 0 applies softcap * tanh(x / softcap)
  * (x clamped to +-15 softcap first). Masked scores never contribute; a row
  * with every key masked yields zeros and lse = -inf.
- * out is contiguous [z, hq, sq, d] (same dtype as q), lse is f32 [z * hq, sq].
+ * out is [z, hq, sq, d] (same dtype as q): contiguous when out_strides is NULL,
+ * else with element strides out_strides (z, h, s, d; d stride 1, others
+ * multiples of 8 — e.g. [z, s, h, d] storage for a following projection).
+ * lse is f32 [z * hq, sq].
  * dtype: GKO_F16 or GKO_BF16; d in {64, 128}.
  */
 int gko_fmha_fwd(int dtype, int64_t z, int64_t hq, int64_t hkv, int64_t sq, int64_t sk, int64_t d,
                  const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
                  const void* v, const int64_t* v_strides, const void* bias, int bias_mode,
-                 int bias_dtype, const int64_t* bias_strides, int64_t bias_batch, float scale,
-                 int causal, int window, float softcap, void* out, float* lse,
-                 unsigned int* status, void* stream);
+                 int bias_dtype, const int64_t* bias_strides, int64_t bias_batch,
+                 const int64_t* out_strides, float scale, int causal, int window, float softcap,
+                 void* out, float* lse, unsigned int* status, void* stream);
 
 /*
  * Fused multi-head attention forward over packed variable-length sequences.
@@ -154,6 +157,33 @@ int gko_fmha_varlen_fwd(int dtype, int64_t b, int64_t hq, int64_t hkv, int64_t d
  */
 int gko_silu_mul(int dtype, int64_t n, const void* x, const void* y, void* out,
                  unsigned int* status, void* stream);
+
+/*
+ * y = rmsnorm(x + residual) * weight over rows of `cols` elements (row stride ld),
+ * rmsnorm(v) = v / sqrt(mean(v^2) + eps). residual may be NULL; when sum_out is
+ * not NULL it receives x + residual (the updated residual stream). bf16/f16,
+ * cols <= 16384, cols and ld multiples of 8.
+ *
+ * No reference counterpart: the RMSNorm of the Llama-3-70B block configuration
+ * (the reference has no transformer block on its kernel path).
+ */
+int gko_rmsnorm(int dtype, int64_t rows, int64_t cols, const void* x, const void* residual,
+                const void* weight, float eps, void* out, void* sum_out, int64_t ld,
+                unsigned int* status, void* stream);
+
+/*
+ * Rotary position embedding, applied in place to `heads` heads of head_dim
+ * elements for each of `tokens` tokens (element strides st_token, st_head),
+ * rotate-half convention: for i < head_dim/2 and f_i = theta^(-2i/head_dim),
+ * (x_i, x_{i+D/2}) <- (x_i cos(p f_i) - x_{i+D/2} sin(p f_i), x_{i+D/2} cos(p f_i) + x_i sin(p f_i)).
+ * The position p of token t is positions[t] (device int32) or, when positions
+ * is NULL, t % seq_len.
+ *
+ * No reference counterpart: the RoPE of the Llama-3-70B block configuration.
+ */
+int gko_rope(int dtype, int64_t tokens, int64_t heads, int64_t head_dim, void* x, int64_t st_token,
+             int64_t st_head, const int32_t* positions, int64_t seq_len, float theta,
+             unsigned int* status, void* stream);
 
 /*
  * Self-test of the failure path (no reference counterpart): launches one CTA

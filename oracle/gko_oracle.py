@@ -29,6 +29,9 @@ __all__ = [
     "silu_mul",
     "attention",
     "attention_varlen",
+    "rmsnorm",
+    "rope",
+    "llama_block",
 ]
 
 
@@ -189,3 +192,46 @@ def rel_err(out, ref) -> float:
 
 def scaled_tolerance_ok(out, ref, rel: float) -> bool:
     return rel_err(out, ref) <= rel and not math.isnan(rel_err(out, ref))
+
+
+def rmsnorm(x, weight, eps=1e-5):
+    """x * rsqrt(mean(x^2) + eps) * weight over the last dim, fp32 (Llama RMSNorm)."""
+    xf = _f32(x)
+    return xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * _f32(weight)
+
+
+def rope(x, theta=500000.0, positions=None):
+    """Rotate-half RoPE (the HF Llama convention) of x [tokens, heads, D] in fp32 at positions[t]."""
+    xf = _f32(x)
+    t, _, d = xf.shape
+    pos = torch.arange(t, dtype=torch.float64) if positions is None else _f32(positions).double()
+    inv_freq = torch.pow(torch.tensor(theta, dtype=torch.float64), -torch.arange(0, d, 2, dtype=torch.float64) / d)
+    ang = (pos[:, None] * inv_freq[None, :]).float()          # [t, D/2]
+    c, s = torch.cos(ang)[:, None, :], torch.sin(ang)[:, None, :]
+    x1, x2 = xf[..., : d // 2], xf[..., d // 2:]
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+
+def llama_block(x, w, cfg):
+    """One Llama transformer block (prefill, causal, GQA) in fp32 on the CPU.
+
+    x [B, S, d]; w holds the full weights (attn_norm, wq, wk, wv, wo, mlp_norm, w_gate, w_up, w_down);
+    cfg has d_model, n_heads, n_kv_heads, head_dim, d_ff, eps, rope_theta. No reference counterpart
+    (the reference's kernel path has no block); this is the standard formulation the fused path computes.
+    """
+    xf = _f32(x)
+    B, S, d = xf.shape
+    hd = cfg.head_dim
+    h = rmsnorm(xf, w["attn_norm"], cfg.eps)
+    q = F.linear(h, _f32(w["wq"])).view(B, S, cfg.n_heads, hd)
+    k = F.linear(h, _f32(w["wk"])).view(B, S, cfg.n_kv_heads, hd)
+    v = F.linear(h, _f32(w["wv"])).view(B, S, cfg.n_kv_heads, hd)
+    pos = torch.arange(S)
+    q = torch.stack([rope(q[b], cfg.rope_theta, pos) for b in range(B)])
+    k = torch.stack([rope(k[b], cfg.rope_theta, pos) for b in range(B)])
+    o, _ = attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), None, hd ** -0.5, 1)
+    o = F.linear(o.transpose(1, 2).reshape(B, S, cfg.n_heads * hd), _f32(w["wo"]))
+    x1 = xf + o
+    h2 = rmsnorm(x1, w["mlp_norm"], cfg.eps)
+    g = F.silu(F.linear(h2, _f32(w["w_gate"]))) * F.linear(h2, _f32(w["w_up"]))
+    return x1 + F.linear(g, _f32(w["w_down"]))

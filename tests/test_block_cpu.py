@@ -1,0 +1,84 @@
+"""Tensor-parallel decomposition of the Llama block on CPU with two gloo ranks: each rank
+computes its shard (column-parallel QKV / gate-up, row-parallel o / down) in fp32 and the
+all-reduced result equals the unsharded block. This covers the host-side partitioning that the
+GPU path (evocompile_b200.block.TPBlock) uses with NCCL."""
+
+import os
+import random
+
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+import torch.nn.functional as F
+
+import oracle
+from evocompile_b200.block import BlockConfig, init_weights, shard_weights
+
+CFG = BlockConfig(d_model=128, n_heads=8, n_kv_heads=4, head_dim=32, d_ff=256)
+
+
+def _tp_forward(local, cfg, x, group):
+    """The TPBlock.forward data flow with fp32 CPU ops and a gloo all-reduce."""
+    B, S, d = x.shape
+    hd, hq, hkv = cfg.head_dim, local["hq_local"], local["hkv_local"]
+    h = oracle.rmsnorm(x, local["attn_norm"], cfg.eps)
+    qkv = F.linear(h, local["wqkv"].float())
+    q = qkv[..., : hq * hd].reshape(B, S, hq, hd)
+    k = qkv[..., hq * hd: (hq + hkv) * hd].reshape(B, S, hkv, hd)
+    v = qkv[..., (hq + hkv) * hd:].reshape(B, S, hkv, hd)
+    q = torch.stack([oracle.rope(q[b], cfg.rope_theta) for b in range(B)])
+    k = torch.stack([oracle.rope(k[b], cfg.rope_theta) for b in range(B)])
+    o, _ = oracle.attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), None, hd ** -0.5, 1)
+    o = F.linear(o.transpose(1, 2).reshape(B, S, hq * hd), local["wo"].float())
+    dist.all_reduce(o, group=group)
+    x1 = x + o
+    h2 = oracle.rmsnorm(x1, local["mlp_norm"], cfg.eps)
+    gu = F.linear(h2, local["w_gate_up"].float())
+    g = F.silu(gu[..., : gu.shape[-1] // 2]) * gu[..., gu.shape[-1] // 2:]
+    dn = F.linear(g, local["w_down"].float())
+    dist.all_reduce(dn, group=group)
+    return x1 + dn
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        full = init_weights(CFG, "cpu", torch.float32, seed=0)
+        x = torch.randn(2, 24, CFG.d_model, generator=torch.Generator().manual_seed(1))
+        y = _tp_forward(shard_weights(full, CFG, rank, world), CFG, x, None)
+        if rank == 0:
+            ref = oracle.llama_block(x, full, CFG)
+            q.put(float((y - ref).abs().max() / ref.abs().max()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_shard_shapes():
+    full = init_weights(CFG, "cpu", torch.float32)
+    for world in (1, 2, 4):
+        loc = shard_weights(full, CFG, 0, world)
+        hd = CFG.head_dim
+        assert loc["wqkv"].shape == ((CFG.n_heads + 2 * CFG.n_kv_heads) // world * hd, CFG.d_model)
+        assert loc["wo"].shape == (CFG.d_model, CFG.n_heads // world * hd)
+        assert loc["w_gate_up"].shape == (2 * CFG.d_ff // world, CFG.d_model)
+        assert loc["w_down"].shape == (CFG.d_model, CFG.d_ff // world)
+
+
+def test_flops_formula():
+    cfg = BlockConfig()
+    assert abs(cfg.flops(16384, 4096) - 2.914e13) / 2.914e13 < 2e-3
+
+
+def test_tp2_matches_unsharded():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 30500 + random.Random().randint(0, 2000)
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    err = q.get(timeout=180)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert err < 1e-5

@@ -1,0 +1,120 @@
+"""The Llama block and its memory-bound kernels (RMSNorm, RoPE) on the GPU against the fp32 CPU
+oracle. bf16 outputs: max|err| / max|ref| <= 2e-2."""
+
+import os
+import random
+
+import pytest
+import torch
+
+import oracle
+from evocompile_b200 import _lib, ops
+from evocompile_b200.block import BlockConfig, TPBlock, init_weights, shard_weights
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-2
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 8), (7, 512), (300, 8192), (5, 16384)])
+@pytest.mark.parametrize("with_res", [False, True])
+def test_rmsnorm(rows, cols, with_res):
+    g = torch.Generator().manual_seed(rows + cols)
+    x = torch.randn(rows, cols, generator=g).to(torch.bfloat16)
+    r = torch.randn(rows, cols, generator=g).to(torch.bfloat16) if with_res else None
+    w = (1 + 0.1 * torch.randn(cols, generator=g)).to(torch.bfloat16)
+    dev = torch.device("cuda", 0)
+    out, tot = ops.rmsnorm(x.to(dev), w.to(dev), 1e-5, residual=None if r is None else r.to(dev), return_sum=True)
+    xs = x.float() + (r.float() if r is not None else 0)
+    assert oracle.rel_err(out, oracle.rmsnorm(xs, w, 1e-5)) <= TOL
+    assert oracle.rel_err(tot, xs) <= 1e-2
+
+
+@pytest.mark.parametrize("heads,d", [(4, 64), (8, 128)])
+def test_rope_strided_in_place(heads, d):
+    g = torch.Generator().manual_seed(heads)
+    T = 300
+    buf = torch.randn(T, heads * 3, d, generator=g).to(torch.bfloat16)   # qkv-like buffer; rope the middle third
+    dev_buf = buf.cuda()
+    view = dev_buf[:, heads: 2 * heads]
+    ops.rope_(view, 500000.0, seq_len=100)
+    ref = oracle.rope(buf[:, heads: 2 * heads].float(), 500000.0, torch.arange(T) % 100)
+    assert oracle.rel_err(dev_buf[:, heads: 2 * heads], ref) <= TOL
+    # the other heads are untouched
+    assert torch.equal(dev_buf[:, :heads].cpu(), buf[:, :heads])
+    assert torch.equal(dev_buf[:, 2 * heads:].cpu(), buf[:, 2 * heads:])
+
+
+def test_fmha_strided_output():
+    g = torch.Generator().manual_seed(0)
+    B, S, H, D = 2, 200, 4, 128
+    q, k, v = (torch.randn(B, S, H, D, generator=g).to(torch.bfloat16) for _ in range(3))
+    dev = torch.device("cuda", 0)
+    out = torch.empty(B, S, H, D, device=dev, dtype=torch.bfloat16)
+    t = lambda x: x.to(dev).transpose(1, 2)  # noqa: E731
+    ops.fmha_fwd(t(q), t(k), t(v), None, D ** -0.5, 1, out=out.transpose(1, 2))
+    ref, _ = oracle.attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), None, D ** -0.5, 1)
+    assert oracle.rel_err(out.transpose(1, 2), ref) <= TOL
+
+
+def _block_check(cfg, B, S, seed=0):
+    dev = torch.device("cuda", 0)
+    full = init_weights(cfg, dev, torch.bfloat16, seed=seed)
+    x = torch.randn(B, S, cfg.d_model, device=dev, generator=torch.Generator(device=dev).manual_seed(seed + 1))
+    x = x.to(torch.bfloat16)
+    blk = TPBlock(shard_weights(full, cfg, 0, 1), cfg)
+    y = blk.forward(x)
+    torch.cuda.synchronize()
+    assert _lib.read_status(dev) == 0
+    ref = oracle.llama_block(x, {k: v for k, v in full.items()}, cfg)
+    return oracle.rel_err(y, ref)
+
+
+def test_block_small():
+    cfg = BlockConfig(d_model=512, n_heads=8, n_kv_heads=2, head_dim=128, d_ff=1024)
+    assert _block_check(cfg, 2, 200) <= TOL
+
+
+@pytest.mark.slow
+def test_block_full_width():
+    """Llama-3-70B widths (d 8192, 64/8 heads, d_ff 28672) on one 512-token sequence."""
+    assert _block_check(BlockConfig(), 1, 512) <= TOL
+
+
+def _tp_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    torch.cuda.set_device(rank)
+    torch.distributed.init_process_group("nccl", rank=rank, world_size=world,
+                                         timeout=datetime.timedelta(seconds=60),
+                                         device_id=torch.device("cuda", rank))
+    try:
+        cfg = BlockConfig(d_model=512, n_heads=8, n_kv_heads=2, head_dim=128, d_ff=1024)
+        dev = torch.device("cuda", rank)
+        full = init_weights(cfg, dev, torch.bfloat16, seed=3)
+        x = torch.randn(2, 160, cfg.d_model, device=dev, generator=torch.Generator(device=dev).manual_seed(4))
+        x = x.to(torch.bfloat16)
+        y = TPBlock(shard_weights(full, cfg, rank, world), cfg, torch.distributed.group.WORLD).forward(x)
+        torch.cuda.synchronize()
+        if rank == 0:
+            ref = oracle.llama_block(x, full, cfg)
+            q.put(oracle.rel_err(y, ref))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_block_tp2_nccl():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 31500 + random.Random().randint(0, 2000)
+    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    err = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert err <= TOL

@@ -80,7 +80,7 @@ def _i64x4(*v):
 def test_fmha_rejects_head_dim_and_dtype(lib):
     st = _i64x4(0, 0, 0, 1)
     args = lambda dt, d, hq=4, hkv=2: (dt, 1, hq, hkv, 16, 16, d, _null(), st, _null(), st, _null(), st, _null(), 0, 0,
-                                      st, 1, 0.1, 0, 0, 0.0, _null(), _null(), _null(), _null())
+                                      st, 1, None, 0.1, 0, 0, 0.0, _null(), _null(), _null(), _null())
     assert lib.gko_fmha_fwd(*args(_lib.BF16, 96)) == _lib.ERR_UNSUPPORTED
     assert "head dim" in _lib.last_error()
     assert lib.gko_fmha_fwd(*args(_lib.F32, 64)) == _lib.ERR_UNSUPPORTED
