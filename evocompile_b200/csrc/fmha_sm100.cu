@@ -44,6 +44,17 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.f;  // log2 units
+// K tiles are double or triple buffered (V always double): the S MMA of the next key tile
+// waits on K, so a deeper K ring hides more TMA latency when shared memory allows it.
+#ifndef GKO_FMHA_K_STAGES
+#define GKO_FMHA_K_STAGES 2
+#endif
+constexpr int kKStages = GKO_FMHA_K_STAGES;
+// Wait for K(j+1) right before the first S MMA that reads it (1) or before the PV MMAs of
+// tile j (0).
+#ifndef GKO_FMHA_LATE_KWAIT
+#define GKO_FMHA_LATE_KWAIT 1
+#endif
 // In tiles without masked keys, pair c of each 8 uses the FMA-pipe exponential when
 // bit (c % 8) is set, the MUFU otherwise (a knob for balancing the two pipes).
 #ifndef GKO_FMHA_POLY_PAIRS
@@ -78,9 +89,9 @@ struct Layout {
   static constexpr uint32_t kChunk = 128 * 128;  // one [128 rows x 128 B] swizzle block
   static constexpr int kChunks = D / 64;
   static constexpr uint32_t kTile = kChunks * kChunk;  // 128 x D elements
-  static constexpr uint32_t kQ = 0;                 // Q0, Q1
-  static constexpr uint32_t kK0 = kQ + 2 * kTile;   // K stages 0, 1
-  static constexpr uint32_t kV0 = kK0 + 2 * kTile;  // V stages 0, 1
+  static constexpr uint32_t kQ = 0;                          // Q0, Q1
+  static constexpr uint32_t kK0 = kQ + 2 * kTile;            // K stages
+  static constexpr uint32_t kV0 = kK0 + kKStages * kTile;    // V stages 0, 1
   static constexpr uint32_t kMeta = kV0 + 2 * kTile;
   // at least 120 KB so that a single CTA (and its 512 TMEM columns) occupies an SM
   static constexpr uint32_t kBytes = (1024 + kMeta + 256) > 122880 ? (1024 + kMeta + 256) : 122880;
@@ -164,27 +175,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* meta = smem_raw + pad + L::kMeta;
   const uint32_t smeta = sb + L::kMeta;
   const uint32_t bar_q = smeta;
-  const uint32_t bar_kfull = smeta + 8;     // [2]
-  const uint32_t bar_kempty = smeta + 24;   // [2]
-  const uint32_t bar_vfull = smeta + 40;    // [2]
-  const uint32_t bar_vempty = smeta + 56;   // [2]
-  const uint32_t bar_sfull = smeta + 72;    // [2] per query tile
+  const uint32_t bar_kfull = smeta + 8;     // [kKStages <= 3]
+  const uint32_t bar_kempty = smeta + 32;   // [kKStages <= 3]
+  const uint32_t bar_vfull = smeta + 56;    // [2]
+  const uint32_t bar_vempty = smeta + 72;   // [2]
+  const uint32_t bar_sfull = smeta + 88;    // [2] per query tile
   // [2 query tiles][2 halves]: P is handed over in two halves; a barrier per half
   // completes once per key tile, so a waiter can never miss a phase.
-  const uint32_t bar_pfull = smeta + 88;
-  const uint32_t bar_ofinal = smeta + 120;  // [2] per query tile
-  const uint32_t bar_drain = smeta + 136;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 144);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 148);
+  const uint32_t bar_pfull = smeta + 104;
+  const uint32_t bar_ofinal = smeta + 136;  // [2] per query tile
+  const uint32_t bar_drain = smeta + 152;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(meta + 160);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(meta + 164);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     mbar_init(bar_q, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kKStages; ++i) {
       mbar_init(bar_kfull + 8 * i, 1);
       mbar_init(bar_kempty + 8 * i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(bar_vfull + 8 * i, 1);
       mbar_init(bar_vempty + 8 * i, 1);
       mbar_init(bar_sfull + 8 * i, 1);
@@ -225,13 +238,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = 0; u < n_tiles; ++u) {
         const int st = u & 1;
         const uint32_t ph = (u >> 1) & 1;
+        const int ks = u % kKStages;
+        const uint32_t kph = (u / kKStages) & 1;
         const int krow = row_k0 + (lo + u) * kBN;
-        if (!wait_bounded(bar_kempty + 8 * st, ph ^ 1, abort_flag, p.status, kStatusTimeoutProducer))
+        if (!wait_bounded(bar_kempty + 8 * ks, kph ^ 1, abort_flag, p.status, kStatusTimeoutProducer))
           break;
-        mbar_arrive_expect_tx(bar_kfull + 8 * st, L::kTile);
+        mbar_arrive_expect_tx(bar_kfull + 8 * ks, L::kTile);
 #pragma unroll
         for (int c = 0; c < L::kChunks; ++c)
-          tma_load_4d(sb + L::kK0 + st * L::kTile + c * L::kChunk, &tm_k, bar_kfull + 8 * st, c * 64,
+          tma_load_4d(sb + L::kK0 + ks * L::kTile + c * L::kChunk, &tm_k, bar_kfull + 8 * ks, c * 64,
                       krow, hk, zc);
         if (!wait_bounded(bar_vempty + 8 * st, ph ^ 1, abort_flag, p.status, kStatusTimeoutProducer))
           break;
@@ -247,8 +262,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0 && n_tiles > 0) {
       bool ok = wait_bounded(bar_q, 0, abort_flag, p.status, kStatusTimeoutMma);
       auto issue_s = [&](int t, int u) {
-        const int st = u & 1;
-        const uint32_t k_addr = sb + L::kK0 + st * L::kTile;
+        const uint32_t k_addr = sb + L::kK0 + (u % kKStages) * L::kTile;
         const uint32_t q_addr = sb + L::kQ + t * L::kTile;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -286,9 +300,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = (u >> 1) & 1;
         ok = wait_bounded(bar_vfull + 8 * st, ph, abort_flag, p.status, kStatusTimeoutMma);
         const bool next = (u + 1 < n_tiles);
-        if (ok && next)
-          ok = wait_bounded(bar_kfull + 8 * ((u + 1) & 1), ((u + 1) >> 1) & 1, abort_flag, p.status,
-                            kStatusTimeoutMma);
+        const int kn = (u + 1) % kKStages;
+        const uint32_t knph = ((u + 1) / kKStages) & 1;
+        bool k_ready = !next;
+        if (!GKO_FMHA_LATE_KWAIT && ok && next) {
+          ok = wait_bounded(bar_kfull + 8 * kn, knph, abort_flag, p.status, kStatusTimeoutMma);
+          k_ready = true;
+        }
         if (!ok) break;
 #pragma unroll
         for (int t = 0; t < kQTiles && ok; ++t) {
@@ -305,11 +323,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             if (j == hi_t[t] - 1) mma_commit(bar_ofinal + 8 * t);
           }
-          if (next && j + 1 >= lo_t[t] && j + 1 < hi_t[t]) issue_s(t, u + 1);
+          if (next && j + 1 >= lo_t[t] && j + 1 < hi_t[t]) {
+            if (!k_ready) {
+              ok = wait_bounded(bar_kfull + 8 * kn, knph, abort_flag, p.status, kStatusTimeoutMma);
+              if (!ok) break;
+              tc_fence_after();
+              k_ready = true;
+            }
+            issue_s(t, u + 1);
+          }
         }
         if (!ok) break;
+        if (next && !k_ready) {  // K(j+1) unused by both tiles: still consume its load before release
+          ok = wait_bounded(bar_kfull + 8 * kn, knph, abort_flag, p.status, kStatusTimeoutMma);
+          if (!ok) break;
+        }
         mma_commit(bar_vempty + 8 * st);
-        if (next) mma_commit(bar_kempty + 8 * ((u + 1) & 1));
+        if (next) mma_commit(bar_kempty + 8 * kn);
       }
       if (*abort_flag) {
         mma_commit(bar_drain);
