@@ -53,6 +53,19 @@ SIGNATURES = {
         [_int, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
          _i64, _vp, _vp, _fl, _int, _int, _fl, _vp, _vp, _vp, _vp],
     ),
+    "gko_fmha_bwd_workspace_size": (_i64, [_i64, _i64, _i64, _i64, _int]),
+    "gko_fmha_bwd": (
+        _int,
+        [_int, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _p64, _vp, _p64, _vp, _p64, _vp, _int, _int,
+         _p64, _i64, _vp, _p64, _vp, _p64, _vp, _fl, _int, _int, _fl, _vp, _p64, _vp, _p64, _vp, _p64,
+         _vp, _i64, _vp, _vp],
+    ),
+    "gko_fmha_varlen_bwd": (
+        _int,
+        [_int, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
+         _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _fl, _int, _int, _fl, _vp, _i64, _i64, _vp,
+         _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp],
+    ),
     "gko_silu_mul": (_int, [_int, _i64, _vp, _vp, _vp, _vp, _vp]),
     "gko_selftest_wait_timeout": (_int, [_vp, ctypes.c_longlong, _vp]),
     "gko_rmsnorm": (_int, [_int, _i64, _i64, _vp, _vp, _vp, _fl, _vp, _vp, _i64, _vp, _vp]),

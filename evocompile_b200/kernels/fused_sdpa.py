@@ -15,10 +15,13 @@ Drop-in for eval/kernels/fused_sdpa.py:
 * ``torch.ops.gko.fmha_varlen_fwd`` — packed variable-length sequences with
   GQA (no reference counterpart).
 
+* ``torch.ops.gko.fmha_varlen_bwd`` — its backward (autograd of
+  ``fmha_varlen_fwd`` is registered).
+
 Additions over the reference Triton path: GQA (k/v with H/g heads) and varlen.
 Supported: float16/bfloat16, D in {64, 128}; anything else raises (there is no
-eager fallback). The backward currently recomputes attention with ATen in
-fp32 from the saved lse (the reference's recompute formulation).
+eager fallback). The backward is the library's tcgen05 kernel (gko_fmha_bwd):
+it recomputes P from the saved lse, as the reference's Triton backward does.
 """
 
 from __future__ import annotations
@@ -31,70 +34,6 @@ from .. import ops
 
 _OP_READY = False
 _AUTOGRADED = False
-
-
-# --------------------------------------------------------------------------- backward (ATen recompute)
-def _softcap_tanh(s, softcap):
-    x = torch.clamp(s / softcap, -15.0, 15.0)
-    return softcap * torch.tanh(x), x
-
-
-def _attention_bwd(q, k, v, attn_bias, out, lse, dout, scale, causal, window, softcap):
-    """dq, dk, dv of softmax(mask(softcap(scale q k^T + bias))) v, from the saved lse.
-
-    Processes one batch entry at a time so the [H, Sq, Sk] score block stays bounded.
-    """
-    z, hq, sq, d = q.shape
-    hkv, sk = k.shape[1], k.shape[2]
-    g = hq // hkv
-    dq = torch.empty_like(q, memory_format=torch.contiguous_format)
-    dk = torch.zeros(k.shape, device=k.device, dtype=torch.float32)
-    dv = torch.zeros(v.shape, device=v.device, dtype=torch.float32)
-    bias_t, mode, bstr, nb = ops._bias_layout(q, k, attn_bias)
-    qi = torch.arange(sq, device=q.device)[:, None]
-    ki = torch.arange(sk, device=q.device)[None, :]
-    keep = torch.ones(sq, sk, dtype=torch.bool, device=q.device)
-    if causal:
-        keep &= ki <= qi
-    if window and window > 0:
-        keep &= (ki - qi <= window) & (qi - ki <= window)
-    lse4 = lse.view(z, hq, sq, 1)
-    for b in range(z):
-        qb = q[b].float()
-        kb = k[b].float().repeat_interleave(g, dim=0)
-        vb = v[b].float().repeat_interleave(g, dim=0)
-        s = torch.matmul(qb, kb.transpose(-1, -2)) * scale
-        if mode != 0:
-            bb = _dense_bias(bias_t, mode, bstr, nb, b, hq, sq, sk)
-            s = s + bb
-        x = None
-        if softcap and softcap > 0:
-            s, x = _softcap_tanh(s, softcap)
-        s = s.masked_fill(~keep, float("-inf"))
-        l = lse4[b]
-        p = torch.exp(s - torch.where(torch.isinf(l), torch.zeros_like(l), l))
-        p = torch.where(torch.isinf(l), torch.zeros_like(p), p)
-        do = dout[b].float()
-        dvb = torch.matmul(p.transpose(-1, -2), do)
-        dp = torch.matmul(do, vb.transpose(-1, -2))
-        delta = (do * out[b].float()).sum(-1, keepdim=True)
-        ds = p * (dp - delta)
-        if x is not None:
-            ds = ds * (1 - torch.tanh(x) ** 2) * ((x > -15.0) & (x < 15.0))
-        dq[b] = (torch.matmul(ds, kb) * scale).to(q.dtype)
-        dkb = torch.matmul(ds.transpose(-1, -2), qb) * scale
-        dk[b] += dkb.view(hkv, g, sk, d).sum(1)
-        dv[b] += dvb.view(hkv, g, sk, d).sum(1)
-    return dq, dk.to(k.dtype), dv.to(v.dtype)
-
-
-def _dense_bias(bias_t, mode, bstr, nb, b, h, sq, sk):
-    bi = b % nb
-    if mode == 1:  # key padding
-        row = torch.as_strided(bias_t, (sk,), (bstr[3],), bias_t.storage_offset() + bi * bstr[0])
-        return row.float().view(1, 1, sk)
-    full = torch.as_strided(bias_t, (h, sq, sk), (bstr[1], bstr[2], bstr[3]), bias_t.storage_offset() + bi * bstr[0])
-    return full.float()
 
 
 # --------------------------------------------------------------------------- python entry points
@@ -142,6 +81,20 @@ def _backward(ctx, grad_out):
     return dq, dk, dv, None, None, None
 
 
+def _setup_varlen(ctx, inputs, output):
+    q, k, v, cu_q, cu_k, max_q, max_k, scale, causal = inputs
+    out, lse = output
+    ctx.save_for_backward(q, k, v, out, lse, cu_q, cu_k)
+    ctx.max_q, ctx.max_k, ctx.scale, ctx.causal = int(max_q), int(max_k), float(scale), int(causal)
+
+
+def _varlen_bwd(ctx, dout, dlse):
+    q, k, v, out, lse, cu_q, cu_k = ctx.saved_tensors
+    dq, dk, dv = torch.ops.gko.fmha_varlen_bwd(q, k, v, out, lse, dout, cu_q, cu_k, ctx.max_q, ctx.max_k,
+                                               ctx.scale, ctx.causal)
+    return dq, dk, dv, None, None, None, None, None, None
+
+
 def _ensure_op():
     global _OP_READY, _AUTOGRADED
     if not _OP_READY:
@@ -165,7 +118,7 @@ def _ensure_op():
             def fused_sdpa_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, attn_bias: torch.Tensor,
                                out: torch.Tensor, lse: torch.Tensor, dout: torch.Tensor, scale: float, causal: int,
                                window: int, softcap: float) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-                return _attention_bwd(q, k, v, attn_bias, out, lse, dout, scale, causal, window, softcap)
+                return ops.fmha_bwd(q, k, v, attn_bias, out, lse, dout, scale, causal, window, softcap)
 
             @fused_sdpa_bwd.register_fake
             def _(q, k, v, attn_bias, out, lse, dout, scale, causal, window, softcap):
@@ -200,6 +153,26 @@ def _ensure_op():
             @fmha_varlen_fwd.register_fake
             def _(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, scale, causal):
                 return q.new_empty(q.shape), q.new_empty((q.size(1), q.size(0)), dtype=torch.float32)
+
+        if not have("fmha_varlen_bwd"):
+
+            @torch.library.custom_op("gko::fmha_varlen_bwd", mutates_args=())
+            def fmha_varlen_bwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,
+                                lse: torch.Tensor, dout: torch.Tensor, cu_seqlens_q: torch.Tensor,
+                                cu_seqlens_k: torch.Tensor, max_seqlen_q: int, max_seqlen_k: int, scale: float,
+                                causal: int) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+                return ops.fmha_varlen_bwd(q, k, v, out, lse, dout, cu_seqlens_q, cu_seqlens_k, max_seqlen_q,
+                                           max_seqlen_k, scale, causal)
+
+            @fmha_varlen_bwd.register_fake
+            def _(q, k, v, out, lse, dout, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, scale, causal):
+                return q.new_empty(q.shape), k.new_empty(k.shape), v.new_empty(v.shape)
+
+        try:
+            torch.library.register_autograd("gko::fmha_varlen_fwd", _varlen_bwd, setup_context=_setup_varlen)
+        except RuntimeError as e:
+            if "already" not in str(e).lower():
+                raise
 
         _OP_READY = True
     if not _AUTOGRADED:

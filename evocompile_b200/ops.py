@@ -337,3 +337,106 @@ def fmha_varlen_fwd(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqle
             )
         _lib.check(rc, "gko_fmha_varlen_fwd")
     return out, lse
+
+
+def _bwd_fix(t):
+    """Unit d stride, other strides multiples of 8 elements, 16-byte aligned (else a contiguous copy)."""
+    if t.stride(-1) != 1 or any(s % 8 for s in t.stride()[:-1]) or t.data_ptr() % 16:
+        return t.contiguous()
+    return t
+
+
+def fmha_bwd(q, k, v, attn_bias, out, lse, dout, scale=None, causal=0, window=0, softcap=0.0):
+    """Fused attention backward -> (dq, dk, dv), contiguous, dtypes of q / k / v.
+
+    Inputs as for ``fmha_fwd`` plus its ``out`` and ``lse`` and the incoming gradient ``dout``
+    [z, hq, sq, d]. Contract of gko::fused_sdpa_bwd (eval/kernels/fused_sdpa.py:945-967); with
+    GQA (hkv < hq) dk/dv sum over each kv head's query group. Bias gets no gradient.
+    """
+    dev = _lib.require_cuda(q, k, v, attn_bias, out, lse, dout)
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise RuntimeError("fmha_bwd: q, k, v must be 4-D [z, h, s, d]")
+    if q.dtype != k.dtype or q.dtype != v.dtype or out.dtype != q.dtype or dout.dtype != q.dtype:
+        raise RuntimeError("fmha_bwd: q, k, v, out, dout dtypes differ")
+    z, hq, sq, d = q.shape
+    _, hkv, sk, dk_ = k.shape
+    if k.shape != v.shape or dk_ != d or k.shape[0] != z:
+        raise RuntimeError(f"fmha_bwd: shape mismatch q={tuple(q.shape)} k={tuple(k.shape)} v={tuple(v.shape)}")
+    if out.shape != q.shape or dout.shape != q.shape:
+        raise RuntimeError("fmha_bwd: out and dout must have q's shape")
+    if lse.dtype != torch.float32 or lse.numel() != z * hq * sq:
+        raise RuntimeError("fmha_bwd: lse must be float32 [z * hq, sq]")
+    if scale is None:
+        scale = d ** -0.5
+    dt = _lib.dtype_code(q.dtype)
+    q, k, v, out, dout = (_bwd_fix(t) for t in (q, k, v, out, dout))
+    lse = lse.contiguous()
+    bias_t, mode, bstr, nb = _bias_layout(q, k, attn_bias)
+    dq = torch.empty((z, hq, sq, d), device=dev, dtype=q.dtype)
+    dk = torch.empty((z, hkv, sk, d), device=dev, dtype=k.dtype)
+    dv = torch.empty((z, hkv, sk, d), device=dev, dtype=v.dtype)
+    if z and hq and (sq or sk):
+        lib = _lib.load()
+        ws_bytes = lib.gko_fmha_bwd_workspace_size(z, hq, sq, d, 0)
+        if ws_bytes < 0:
+            _lib.check(_lib.ERR_UNSUPPORTED, "gko_fmha_bwd_workspace_size")
+        ws = torch.empty(max(ws_bytes, 16), device=dev, dtype=torch.uint8)
+        with torch.cuda.device(dev):
+            rc = lib.gko_fmha_bwd(
+                dt, z, hq, hkv, sq, sk, d,
+                _ptr(q), _I64x4(*q.stride()), _ptr(k), _I64x4(*k.stride()), _ptr(v), _I64x4(*v.stride()),
+                _ptr(bias_t), mode, _lib.dtype_code(bias_t.dtype) if bias_t is not None else 0,
+                _I64x4(*bstr), nb, _ptr(out), _I64x4(*out.stride()), _ptr(dout), _I64x4(*dout.stride()),
+                _ptr(lse), float(scale), int(bool(causal)), int(window or 0), float(softcap or 0.0),
+                _ptr(dq), _I64x4(*dq.stride()), _ptr(dk), _I64x4(*dk.stride()), _ptr(dv), _I64x4(*dv.stride()),
+                _ptr(ws), ws_bytes, _status_ptr(dev), _stream(dev),
+            )
+        _lib.check(rc, "gko_fmha_bwd")
+    return dq, dk, dv
+
+
+def fmha_varlen_bwd(q, k, v, out, lse, dout, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, scale=None,
+                    causal=0, window=0, softcap=0.0):
+    """Backward of ``fmha_varlen_fwd`` -> (dq [tq, hq, d], dk, dv [tk, hkv, d])."""
+    dev = _lib.require_cuda(q, k, v, out, lse, dout, cu_seqlens_q, cu_seqlens_k)
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
+        raise RuntimeError("fmha_varlen_bwd: q, k, v must be 3-D [tokens, heads, d]")
+    if q.dtype != k.dtype or q.dtype != v.dtype or out.dtype != q.dtype or dout.dtype != q.dtype:
+        raise RuntimeError("fmha_varlen_bwd: q, k, v, out, dout dtypes differ")
+    if cu_seqlens_q.dtype != torch.int32 or cu_seqlens_k.dtype != torch.int32:
+        raise RuntimeError("fmha_varlen_bwd: cu_seqlens must be int32")
+    if cu_seqlens_q.numel() != cu_seqlens_k.numel() or cu_seqlens_q.numel() < 1:
+        raise RuntimeError("fmha_varlen_bwd: cu_seqlens_q and cu_seqlens_k must both have b + 1 entries")
+    tq, hq, d = q.shape
+    tk, hkv, dk_ = k.shape
+    if k.shape != v.shape or dk_ != d or out.shape != q.shape or dout.shape != q.shape:
+        raise RuntimeError(f"fmha_varlen_bwd: shape mismatch q={tuple(q.shape)} k={tuple(k.shape)}")
+    if lse.dtype != torch.float32 or lse.numel() != hq * tq:
+        raise RuntimeError("fmha_varlen_bwd: lse must be float32 [hq, tq]")
+    if scale is None:
+        scale = d ** -0.5
+    b = cu_seqlens_q.numel() - 1
+    q, k, v, out, dout = (_bwd_fix(t) for t in (q, k, v, out, dout))
+    lse = lse.contiguous()
+    cq = cu_seqlens_q.contiguous()
+    ck = cu_seqlens_k.contiguous()
+    dq = torch.empty((tq, hq, d), device=dev, dtype=q.dtype)
+    dk = torch.empty((tk, hkv, d), device=dev, dtype=k.dtype)
+    dv = torch.empty((tk, hkv, d), device=dev, dtype=v.dtype)
+    if b and hq and (tq or tk):
+        lib = _lib.load()
+        ws_bytes = lib.gko_fmha_bwd_workspace_size(b, hq, tq, d, 1)
+        if ws_bytes < 0:
+            _lib.check(_lib.ERR_UNSUPPORTED, "gko_fmha_bwd_workspace_size")
+        ws = torch.empty(max(ws_bytes, 16), device=dev, dtype=torch.uint8)
+        with torch.cuda.device(dev):
+            rc = lib.gko_fmha_varlen_bwd(
+                _lib.dtype_code(q.dtype), b, hq, hkv, d, tq, tk, int(max_seqlen_q), int(max_seqlen_k),
+                _ptr(q), q.stride(0), q.stride(1), _ptr(k), k.stride(0), k.stride(1), _ptr(v), v.stride(0),
+                v.stride(1), _ptr(out), out.stride(0), out.stride(1), _ptr(dout), dout.stride(0), dout.stride(1),
+                _ptr(lse), _ptr(cq), _ptr(ck), float(scale), int(bool(causal)), int(window or 0),
+                float(softcap or 0.0), _ptr(dq), dq.stride(0), dq.stride(1), _ptr(dk), dk.stride(0), dk.stride(1),
+                _ptr(dv), dv.stride(0), dv.stride(1), _ptr(ws), ws_bytes, _status_ptr(dev), _stream(dev),
+            )
+        _lib.check(rc, "gko_fmha_varlen_bwd")
+    return dq, dk, dv

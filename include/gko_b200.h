@@ -150,6 +150,55 @@ int gko_fmha_varlen_fwd(int dtype, int64_t b, int64_t hq, int64_t hkv, int64_t d
                         float softcap, void* out, float* lse, unsigned int* status, void* stream);
 
 /*
+ * Bytes of device workspace gko_fmha_bwd (varlen = 0: batch z, per-batch query
+ * length sq_or_tq) or gko_fmha_varlen_bwd (varlen = 1: batch = sequences, sq_or_tq =
+ * total query tokens) needs for head dim d; -1 for invalid sizes. The workspace holds
+ * the fp32 dq accumulator and two f32 per query row.
+ */
+int64_t gko_fmha_bwd_workspace_size(int64_t batch, int64_t hq, int64_t sq_or_tq, int64_t d, int varlen);
+
+/*
+ * Fused multi-head attention backward: dq, dk, dv of gko_fmha_fwd's function.
+ *
+ * Replaces the Triton launches of _triton_bwd (eval/kernels/fused_sdpa.py:668-770:
+ * _flash_bwd_pre, _flash_bwd_dq, _flash_bwd_dkdv at :159-496) behind
+ * gko::fused_sdpa_bwd (eval/kernels/fused_sdpa.py:945-967). Arguments as for
+ * gko_fmha_fwd, plus the forward output `out`, its lse (f32 [z * hq, sq]) and
+ * dout, each [z, h, s, d] with element strides (d stride 1, others multiples of 8).
+ * dq [z, hq, sq, d], dk and dv [z, hkv, sk, d] are written (any strides of the same
+ * rules); with GQA dk/dv sum over each kv head's query group. `workspace` is
+ * device memory of at least gko_fmha_bwd_workspace_size(z, hq, sq, d, 0) bytes,
+ * 16-byte aligned; the call overwrites it. Three kernels on `stream`.
+ */
+int gko_fmha_bwd(int dtype, int64_t z, int64_t hq, int64_t hkv, int64_t sq, int64_t sk, int64_t d,
+                 const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                 const void* v, const int64_t* v_strides, const void* bias, int bias_mode,
+                 int bias_dtype, const int64_t* bias_strides, int64_t bias_batch, const void* out,
+                 const int64_t* out_strides, const void* dout, const int64_t* dout_strides,
+                 const float* lse, float scale, int causal, int window, float softcap, void* dq,
+                 const int64_t* dq_strides, void* dk, const int64_t* dk_strides, void* dv,
+                 const int64_t* dv_strides, void* workspace, int64_t workspace_bytes,
+                 unsigned int* status, void* stream);
+
+/*
+ * Backward of gko_fmha_varlen_fwd (no reference counterpart, like the forward).
+ * Packed tensors [tokens, heads, d] with element strides (token, head): q, out, dout,
+ * dq over tq query tokens and hq heads; k, v, dk, dv over tk key tokens and hkv heads.
+ * lse is f32 [hq, tq]; max_seqlen_q / max_seqlen_k bound the sequence lengths.
+ * workspace: gko_fmha_bwd_workspace_size(b, hq, tq, d, 1) bytes.
+ */
+int gko_fmha_varlen_bwd(int dtype, int64_t b, int64_t hq, int64_t hkv, int64_t d, int64_t tq,
+                        int64_t tk, int64_t max_seqlen_q, int64_t max_seqlen_k, const void* q,
+                        int64_t q_st, int64_t q_sh, const void* k, int64_t k_st, int64_t k_sh,
+                        const void* v, int64_t v_st, int64_t v_sh, const void* out, int64_t o_st,
+                        int64_t o_sh, const void* dout, int64_t do_st, int64_t do_sh,
+                        const float* lse, const int32_t* cu_seqlens_q, const int32_t* cu_seqlens_k,
+                        float scale, int causal, int window, float softcap, void* dq,
+                        int64_t dq_st, int64_t dq_sh, void* dk, int64_t dk_st, int64_t dk_sh,
+                        void* dv, int64_t dv_st, int64_t dv_sh, void* workspace,
+                        int64_t workspace_bytes, unsigned int* status, void* stream);
+
+/*
  * out[i] = silu(x[i]) * y[i] over n contiguous elements (dtype f16, bf16 or f32).
  *
  * Replaces the Triton launch _triton (eval/kernels/silu_mul.py:33-43) behind

@@ -29,6 +29,8 @@ __all__ = [
     "silu_mul",
     "attention",
     "attention_varlen",
+    "attention_bwd",
+    "attention_varlen_bwd",
     "rmsnorm",
     "rope",
     "llama_block",
@@ -36,7 +38,8 @@ __all__ = [
 
 
 def _f32(t):
-    return None if t is None else t.detach().to("cpu", torch.float32)
+    # no detach: the backward restatements differentiate through these functions
+    return None if t is None else t.to("cpu", torch.float32)
 
 
 def addmm_act(bias, mat1, mat2, act: str = "gelu"):
@@ -178,6 +181,32 @@ def attention_varlen(q, k, v, cu_seqlens_q, cu_seqlens_k, scale=None, causal=0, 
         out[q0:q1] = o[0].transpose(0, 1)
         lse[:, q0:q1] = l.reshape(hq, q1 - q0)
     return out, lse
+
+
+def attention_bwd(q, k, v, dout, attn_bias=None, scale=None, causal=0, window=0, softcap=0.0):
+    """(dq, dk, dv) in fp32 for upstream gradient ``dout`` of ``attention``'s output.
+
+    Autograd of the fp32 restatement above, i.e. the math the reference's backward
+    kernels compute (eval/kernels/fused_sdpa.py:159-496 with the launch sequence of
+    _triton_bwd at :668-770): delta = rowsum(O dO), P = exp(logits - lse),
+    dv = P^T dO, dS = P (dP - delta) (times the softcap derivative), dq = scale dS k,
+    dk = scale dS^T q. GQA gradients sum over each kv head's query group. The bias
+    gets no gradient (the reference returns None for it, :865-870).
+    """
+    qf, kf, vf = (_f32(t).clone().requires_grad_(True) for t in (q, k, v))
+    with torch.enable_grad():
+        out, _ = attention(qf, kf, vf, attn_bias, scale, causal, window, softcap)
+        out.backward(_f32(dout))
+    return qf.grad, kf.grad, vf.grad
+
+
+def attention_varlen_bwd(q, k, v, dout, cu_seqlens_q, cu_seqlens_k, scale=None, causal=0, window=0, softcap=0.0):
+    """(dq, dk, dv) in fp32 of ``attention_varlen`` for upstream gradient ``dout`` (autograd)."""
+    qf, kf, vf = (_f32(t).clone().requires_grad_(True) for t in (q, k, v))
+    with torch.enable_grad():
+        out, _ = attention_varlen(qf, kf, vf, cu_seqlens_q, cu_seqlens_k, scale, causal, window, softcap)
+        out.backward(_f32(dout))
+    return qf.grad, kf.grad, vf.grad
 
 
 def rel_err(out, ref) -> float:
