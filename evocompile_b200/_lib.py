@@ -60,6 +60,12 @@ SIGNATURES = {
          _p64, _i64, _vp, _p64, _vp, _p64, _vp, _fl, _int, _int, _fl, _vp, _p64, _vp, _p64, _vp, _p64,
          _vp, _i64, _vp, _vp],
     ),
+    "gko_fmha_bwd_noalloc": (
+        _int,
+        [_int, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _p64, _vp, _p64, _vp, _p64, _vp, _int, _int,
+         _p64, _i64, _vp, _p64, _vp, _p64, _vp, _fl, _int, _int, _fl, _vp, _p64, _vp, _p64, _vp, _p64,
+         _vp, _vp],
+    ),
     "gko_fmha_varlen_bwd": (
         _int,
         [_int, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64,

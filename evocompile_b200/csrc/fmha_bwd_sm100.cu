@@ -37,6 +37,7 @@
 // bulk reduction copies that layout verbatim and the convert kernel undoes it.
 // Registers: 12 warps x 168 at launch; warps 0-3 rise to 248, 4-7 drop to 160, 8-11
 // to 96 (128 x (248 + 160 + 96) = 64512 = 384 x 168).
+#include <mutex>
 #include <type_traits>
 
 #include "host_common.h"
@@ -1019,4 +1020,68 @@ extern "C" int gko_fmha_varlen_bwd(int dtype, int64_t b, int64_t hq, int64_t hkv
   const int kv_tiles = (int)((max_seqlen_k + fmha_bwd::kBN - 1) / fmha_bwd::kBN);
   return fmha_bwd::dispatch<true>(dtype, (int)d, mq, mk, mv, mdo, p, rp, q_blocks, kv_tiles, extra,
                                   reinterpret_cast<cudaStream_t>(stream));
+}
+
+// ------------------------------------------------------------------ allocation-free variant
+// gko_fmha_bwd_noalloc runs the same three kernels as gko_fmha_bwd, with the
+// workspace taken from this fixed device array instead of the caller. The array
+// is part of the library's device image, so every GPU that loads the library
+// holds these 32 MiB until the process exits.
+namespace {
+constexpr int64_t kNoAllocScratchBytes = 32ll << 20;
+static __device__ __align__(256) unsigned char g_fmha_bwd_scratch[kNoAllocScratchBytes];
+
+// Device address of g_fmha_bwd_scratch on the current device. In host code the
+// array's name only stands in for the symbol; the address kernels need comes from
+// cudaGetSymbolAddress, looked up once per device (with that device current).
+void* noalloc_scratch() {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    host::cuda_check(e, "cudaGetDevice");
+    return nullptr;
+  }
+  if (dev < 0 || dev >= 64) {
+    host::fail(GKO_ERR_UNSUPPORTED, "device index %d out of range", dev);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_fmha_bwd_scratch);
+    if (e != cudaSuccess || !p) {
+      host::cuda_check(e != cudaSuccess ? e : cudaErrorInvalidSymbol, "cudaGetSymbolAddress(fmha bwd scratch)");
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+}  // namespace
+
+extern "C" int gko_fmha_bwd_noalloc(int dtype, int64_t z, int64_t hq, int64_t hkv, int64_t sq, int64_t sk, int64_t d,
+                                    const void* q, const int64_t* qs, const void* k, const int64_t* ks,
+                                    const void* v, const int64_t* vs, const void* bias, int bias_mode,
+                                    int bias_dtype, const int64_t* bs, int64_t bias_batch, const void* out,
+                                    const int64_t* os, const void* dout, const int64_t* dos, const float* lse,
+                                    float scale, int causal, int window, float softcap, void* dq,
+                                    const int64_t* dqs, void* dk, const int64_t* dks, void* dv,
+                                    const int64_t* dvs, unsigned int* status, void* stream) {
+  const int64_t need = gko_fmha_bwd_workspace_size(z, hq, sq, d, 0);
+  if (need < 0) return fail(GKO_ERR_INVALID, "fmha backward: bad sizes (z %lld, hq %lld, sq %lld, d %lld)",
+                            (long long)z, (long long)hq, (long long)sq, (long long)d);
+  if (need > kNoAllocScratchBytes)
+    return fail(GKO_ERR_UNSUPPORTED,
+                "gko_fmha_bwd_noalloc: this problem needs %lld bytes of scratch, more than the library's fixed "
+                "%lld bytes (z * hq * ceil(sq / 64) must stay within %lld blocks at d = %lld); call gko_fmha_bwd "
+                "with a caller-provided workspace instead",
+                (long long)need, (long long)kNoAllocScratchBytes,
+                (long long)(kNoAllocScratchBytes / (fmha_bwd::kBM * d * 4 + 2 * fmha_bwd::kBM * 4)), (long long)d);
+  void* scratch = noalloc_scratch();
+  if (!scratch) return GKO_ERR_CUDA;
+  return gko_fmha_bwd(dtype, z, hq, hkv, sq, sk, d, q, qs, k, ks, v, vs, bias, bias_mode, bias_dtype, bs, bias_batch,
+                      out, os, dout, dos, lse, scale, causal, window, softcap, dq, dqs, dk, dks, dv, dvs, scratch,
+                      kNoAllocScratchBytes, status, stream);
 }

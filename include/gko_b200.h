@@ -181,6 +181,34 @@ int gko_fmha_bwd(int dtype, int64_t z, int64_t hq, int64_t hkv, int64_t sq, int6
                  unsigned int* status, void* stream);
 
 /*
+ * gko_fmha_bwd for callers that cannot allocate device memory: no workspace
+ * argument, and no cudaMalloc / cudaFree or other allocating call inside.
+ *
+ * No counterpart in the reference. It exists for callers that cannot supply
+ * gko_fmha_bwd's workspace: a host program whose device memory is reserved by
+ * another runtime's pool, or code that must not pay the implicit device-wide
+ * synchronisation of cudaMalloc / cudaFree, or a plain C caller with no allocator
+ * of its own. The workspace comes instead from a fixed 32 MiB array in the
+ * library's device image, which every GPU that loads the library holds until the
+ * process exits. Limit: gko_fmha_bwd_workspace_size(z, hq, sq, d, 0) <= 32 MiB,
+ * i.e. z * hq * ceil(sq / 64) <= 1008 blocks at d = 128 (1985 at d = 64); larger
+ * problems are rejected with GKO_ERR_UNSUPPORTED. The first call on each device
+ * looks up the array's device address (cudaGetSymbolAddress), so make that first
+ * call before any stream capture. All calls share the one array (each call clears
+ * the parts it uses): calls that overlap on the GPU, on any stream, race and give
+ * wrong results. Arguments and results as for gko_fmha_bwd.
+ */
+int gko_fmha_bwd_noalloc(int dtype, int64_t z, int64_t hq, int64_t hkv, int64_t sq, int64_t sk,
+                         int64_t d, const void* q, const int64_t* q_strides, const void* k,
+                         const int64_t* k_strides, const void* v, const int64_t* v_strides,
+                         const void* bias, int bias_mode, int bias_dtype,
+                         const int64_t* bias_strides, int64_t bias_batch, const void* out,
+                         const int64_t* out_strides, const void* dout, const int64_t* dout_strides,
+                         const float* lse, float scale, int causal, int window, float softcap,
+                         void* dq, const int64_t* dq_strides, void* dk, const int64_t* dk_strides,
+                         void* dv, const int64_t* dv_strides, unsigned int* status, void* stream);
+
+/*
  * Backward of gko_fmha_varlen_fwd (no reference counterpart, like the forward).
  * Packed tensors [tokens, heads, d] with element strides (token, head): q, out, dout,
  * dq over tq query tokens and hq heads; k, v, dk, dv over tk key tokens and hkv heads.
