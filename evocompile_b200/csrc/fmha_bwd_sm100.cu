@@ -11,32 +11,37 @@
 //   1. prep      one CTA per 64-query block: -delta and -lse*log2(e) into the
 //                workspace (padded rows get 0 / -inf, so they contribute nothing),
 //                and zeroes the block's fp32 dq accumulator.
-//   2. main      one CTA per 128-key tile of one kv head. K and V stay in shared
-//                memory; the CTA steps over every (query head of the GQA group,
-//                64-query block) the masks allow:
-//       warp 8     TMA producer: K, V once; Q_j, dO_j, -lse_j, -delta_j per step (3 stages)
-//       warp 9     MMA issuer. Per step j (TMEM columns):
-//                    S^T_j  = K Q_j^T         [256 + 64 (j & 1), 64 cols]
-//                    dP^T_j = V dO_j^T        [384, 64 cols]
-//                    dV    += P^T_j dO_j      [0, D)      A = P^T from TMEM (TS form)
-//                    dK    += dS^T_j Q_j      [128, +D)   A = dS^T from TMEM
-//                    dQ^T_j = K^T dS^T_j      [448, 64 cols]  both operands MN-major in smem
-//                  S^T_{j+1} is issued before dV_j so the tensor core has work while
-//                  warps 0-3 compute P_j.
-//       warps 0-3  one thread per key row: P^T_j = 2^(s * scale * log2 e - lse_j * log2 e)
-//                  written back over S^T_j as bf16/f16 pairs; then dS^T_j into the dP^T
-//                  columns (for dK) and into a swizzled smem tile (for dQ).
-//       warps 4-7  one thread per head-dim row of dQ^T_j: TMEM -> smem (two 16-KB halves)
-//                  -> cp.reduce.async.bulk add.f32 into the workspace accumulator.
-//       At the end warps 0-3 write dk = scale * dK and warps 4-7 write dv from TMEM.
+//   2. main      one CTA per 128-key tile of one kv head; it steps over every (query
+//                head of the GQA group, 64-query block) the masks allow.
 //   3. convert   dq = scale * accumulator, cast to the input dtype.
 //
-// The fp32 dq accumulator is laid out per 64-query block as two halves of
-// [D rows][32 queries], each 128-byte row with its 16-byte chunks XOR-swizzled by
-// (row & 7) so that the warpgroup's shared-memory stores are conflict free; the
-// bulk reduction copies that layout verbatim and the convert kernel undoes it.
-// Registers: 12 warps x 168 at launch; warps 0-3 rise to 248, 4-7 drop to 160, 8-11
-// to 96 (128 x (248 + 160 + 96) = 64512 = 384 x 168).
+// The main kernel is laid out around two costs of B200: shared-memory bandwidth
+// (about 128 B per clock per SM, which limits MMAs that read both operands from shared
+// memory at N <= 64) and the latency of a hand-off between warps through an mbarrier
+// (a few hundred cycles, more after a tcgen05.commit). K is copied once into TMEM and is
+// the A operand (TS form) of S^T = K Q^T; dV and dK take P^T / dS^T from TMEM; dQ^T has
+// its own TMEM buffer, so the MMA for the next step's dP^T never waits for dQ^T to be
+// drained, and the dS^T smem tile is double buffered. dQ^T leaves TMEM through registers
+// as fp32 reductions into L2 (no shared-memory staging).
+// TMEM columns: K [0, 64)  dQ^T [64, 128)  dV [128, 256)  dK [256, 384)
+//               S^T|P^T [384, 448)  dP^T|dS^T [448, 512)
+//   warp 13    MMA issuer. Step j, in issue order:
+//                dV += P^T_j dO_j        (A = P^T in TMEM, B = dO_j MN-major)
+//                S^T_{j+1} = K Q_{j+1}^T (A = K in TMEM) — the S columns are free once dV_j is issued
+//                dK += dS^T_j Q_j        (A = dS^T in TMEM)
+//                dP^T_{j+1} = V dO_{j+1}^T (both from smem) — the dP columns are free once dK_j is issued
+//                dQ^T_j = K^T dS^T_j     (both from smem, MN-major) once warps 8-11 have read dQ^T_{j-1}
+//   warp 12    TMA producer: K, V once; Q_j, dO_j, -lse_j, -delta_j per step (3 stages).
+//   warps 0-7  compute: warp w owns key rows 32 (w & 3) .. +31 (its TMEM lane quarter) and
+//              query columns 32 (w >> 2) .. +31: first K (w < 4) into TMEM; then per step
+//              P^T = 2^(s * scale * log2 e - lse * log2 e) over S^T (bf16/f16 pairs) and
+//              dS^T = P^T (dP^T - delta) over dP^T and into smem dS tile j & 1.
+//              At the end dk = scale * dK (half the columns each).
+//   warps 8-11 one head-dim row of dQ^T_j per thread: 64 fp32 reductions (red.global.add)
+//              into the row-major [queries][D] accumulator; at the end dv = dV.
+// Registers: 16 warps x 128 at launch; the compute warpgroups rise to 152, the drain
+// warpgroup drops to 112 and the producer/MMA warpgroup to 96
+// (128 x (2 x 152 + 112 + 96) = 65536 = 512 x 128).
 #include <mutex>
 #include <type_traits>
 
@@ -48,16 +53,17 @@ namespace fmha_bwd {
 
 constexpr int kBN = 128;  // keys per CTA (one per TMEM lane)
 constexpr int kBM = 64;   // queries per step
-constexpr int kThreads = 384;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kThreads = 512;
+constexpr int kDrainWarp0 = 8;
+constexpr int kProducerWarp = 12;
+constexpr int kMmaWarp = 13;
 constexpr int kStages = 3;
-constexpr uint32_t kRegsCompute = 248;
-constexpr uint32_t kRegsDrain = 160;
+constexpr uint32_t kRegsCompute = 152;
+constexpr uint32_t kRegsDrain = 112;
 constexpr uint32_t kRegsControl = 96;
-static_assert(128 * (kRegsCompute + kRegsDrain + kRegsControl) <= 384 * 168, "register split exceeds the launch");
+static_assert(128 * (2 * kRegsCompute + kRegsDrain + kRegsControl) <= 512 * 128, "register split exceeds the launch");
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmDV = 0, kTmDK = 128, kTmS = 256, kTmDP = 384, kTmDQ = 448;
+constexpr uint32_t kTmK = 0, kTmDQ = 64, kTmDV = 128, kTmDK = 256, kTmS = 384, kTmDP = 448;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct Params {
@@ -69,8 +75,8 @@ struct Params {
   const void* bias;
   int bias_mode, bias_dtype, bias_z;
   int64_t b_sz, b_sh, b_sq, b_sk;
-  // workspace, indexed by 64-query block ("tile"); see tile_index
-  float* dq_acc;      // [tiles][64 * D]
+  // workspace, indexed by 64-query block ("tile": per head, consecutive blocks of rows)
+  float* dq_acc;      // [tiles][64 queries][D], row-major fp32
   const float* nl;    // [tiles][64]  -lse * log2(e), -inf for padded / empty rows
   const float* nd;    // [tiles][64]  -rowsum(O * dO)
   int64_t tiles_per_head;
@@ -125,15 +131,15 @@ struct Layout {
   static constexpr uint32_t kTileQ = (D / 64) * kChunkQ;
   static constexpr uint32_t kK = 0;
   static constexpr uint32_t kV = kTileKV;
-  static constexpr uint32_t kStage0 = 2 * kTileKV;
-  static constexpr uint32_t kStQ = 0, kStDO = kTileQ, kStNL = 2 * kTileQ, kStND = 2 * kTileQ + 256;
-  static constexpr uint32_t kStageBytes = ((2 * kTileQ + 512 + 1023) / 1024) * 1024;
-  static constexpr uint32_t kDS = kStage0 + kStages * kStageBytes;  // [128 keys][64 q] bf16, SW128
-  static constexpr uint32_t kDQ = kDS + kBN * 128;                  // 2 x [D][32] f32
-  static constexpr uint32_t kDQHalf = D * 32 * 4;
-  static constexpr uint32_t kMeta = kDQ + 2 * kDQHalf;
+  static constexpr uint32_t kStage0 = 2 * kTileKV;  // stage s: Q at +0, dO at +kTileQ
+  static constexpr uint32_t kStageBytes = 2 * kTileQ;
+  static constexpr uint32_t kDS = kStage0 + kStages * kStageBytes;  // 2 x [128 keys][64 q] bf16, SW128
+  static constexpr uint32_t kDSBytes = kBN * 128;
+  static constexpr uint32_t kRow = kDS + 2 * kDSBytes;  // per stage: -lse log2 e [64], -delta [64]
+  static constexpr uint32_t kMeta = kRow + kStages * 512;
   static constexpr uint32_t kBytes = (1024 + kMeta + 256) > 122880 ? (1024 + kMeta + 256) : 122880;
   static_assert(kDS % 1024 == 0 && kStageBytes % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+  static_assert(1024 + kMeta + 256 <= 232448, "shared memory budget");
 };
 
 template <typename T, int D, bool VARLEN, bool EXTRA>
@@ -143,9 +149,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const Params p) {
   using L = Layout<D>;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t kIdescS = make_idesc_f16(kBF16, kBN, kBM, false, false);   // S^T, dP^T
-  constexpr uint32_t kIdescKV = make_idesc_f16(kBF16, kBN, D, false, true);     // dV, dK
-  constexpr uint32_t kIdescQ = make_idesc_f16(kBF16, 128, kBM, true, true);     // dQ^T
+  constexpr uint32_t kIdescS = make_idesc_f16(kBF16, kBN, kBM, false, false);  // S^T, dP^T
+  constexpr uint32_t kIdescKV = make_idesc_f16(kBF16, kBN, D, false, true);    // dV, dK
+  constexpr uint32_t kIdescQ = make_idesc_f16(kBF16, 128, kBM, true, true);    // dQ^T
 
   // ---------------------------------------------------------- block geometry
   const int bh = (int)blockIdx.y + (int)blockIdx.z * (int)gridDim.y;
@@ -212,44 +218,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sb = raw_addr + pad;
   uint8_t* sgen = smem_raw + pad;  // generic pointer to the same base
   const uint32_t smeta = sb + L::kMeta;
-  const uint32_t bar_kv = smeta;
-  const uint32_t bar_full = smeta + 8;    // [3]
-  const uint32_t bar_empty = smeta + 32;  // [3]
-  const uint32_t bar_sfull = smeta + 56;  // [2] per S buffer
-  const uint32_t bar_pfull = smeta + 72;  // [2] per S buffer, 4 arrivals
-  const uint32_t bar_dpfull = smeta + 88;
-  const uint32_t bar_dsfull = smeta + 96;  // 4 arrivals
-  const uint32_t bar_dqfull = smeta + 104;
-  const uint32_t bar_dqempty = smeta + 112;  // 4 arrivals
-  const uint32_t bar_final = smeta + 120;
-  const uint32_t bar_drain = smeta + 128;
-  // dQ staging handshake inside warps 4-7, per half buffer: `free` (the previous bulk
-  // reduction has read the buffer; 1 arrival) and `written` (128 arrivals).
-  const uint32_t bar_free = smeta + 136;     // [2]
-  const uint32_t bar_written = smeta + 152;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + L::kMeta + 168);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + L::kMeta + 172);
+  const uint32_t bar_kv = smeta;            // K, V landed in smem (TMA)
+  const uint32_t bar_kvtm = smeta + 8;      // K copied into TMEM (4 arrivals)
+  const uint32_t bar_full = smeta + 16;     // [3]
+  const uint32_t bar_empty = smeta + 40;    // [3]
+  const uint32_t bar_sfull = smeta + 64;
+  const uint32_t bar_pfull = smeta + 72;    // 8 arrivals
+  const uint32_t bar_dpfull = smeta + 80;
+  const uint32_t bar_dsfull = smeta + 88;   // 8 arrivals
+  const uint32_t bar_dqfull = smeta + 96;
+  const uint32_t bar_dqempty = smeta + 104;  // 4 arrivals
+  const uint32_t bar_dsfree = smeta + 112;   // [2] per smem dS tile: dQ^T has read it
+  const uint32_t bar_final = smeta + 128;
+  const uint32_t bar_drain = smeta + 136;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sgen + L::kMeta + 144);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(sgen + L::kMeta + 148);
 
   if (threadIdx.x == 0) {
     mbar_init(bar_kv, 1);
+    mbar_init(bar_kvtm, 4);
     for (int i = 0; i < kStages; ++i) {
       mbar_init(bar_full + 8 * i, 1);
       mbar_init(bar_empty + 8 * i, 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bar_sfull + 8 * i, 1);
-      mbar_init(bar_pfull + 8 * i, 4);
-    }
+    mbar_init(bar_sfull, 1);
+    mbar_init(bar_pfull, 8);
     mbar_init(bar_dpfull, 1);
-    mbar_init(bar_dsfull, 4);
+    mbar_init(bar_dsfull, 8);
     mbar_init(bar_dqfull, 1);
     mbar_init(bar_dqempty, 4);
+    mbar_init(bar_dsfree, 1);
+    mbar_init(bar_dsfree + 8, 1);
     mbar_init(bar_final, 1);
     mbar_init(bar_drain, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bar_free + 8 * i, 1);
-      mbar_init(bar_written + 8 * i, 128);
-    }
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tm_q);
@@ -288,44 +289,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(full, 2 * L::kTileQ + 512);
 #pragma unroll
           for (int c = 0; c < D / 64; ++c) {
-            tma_load_4d(stage + L::kStQ + c * L::kChunkQ, &tm_q, full, c * 64, row_q0 + jb * kBM,
-                        hk * p.group + hh, zc);
-            tma_load_4d(stage + L::kStDO + c * L::kChunkQ, &tm_do, full, c * 64, row_q0 + jb * kBM,
+            tma_load_4d(stage + c * L::kChunkQ, &tm_q, full, c * 64, row_q0 + jb * kBM, hk * p.group + hh, zc);
+            tma_load_4d(stage + L::kTileQ + c * L::kChunkQ, &tm_do, full, c * 64, row_q0 + jb * kBM,
                         hk * p.group + hh, zc);
           }
           const int64_t t = tile_of(hh, jb);
-          bulk_load(stage + L::kStNL, p.nl + t * kBM, kBM * 4, full);
-          bulk_load(stage + L::kStND, p.nd + t * kBM, kBM * 4, full);
+          bulk_load(sb + L::kRow + st * 512, p.nl + t * kBM, kBM * 4, full);
+          bulk_load(sb + L::kRow + st * 512 + 256, p.nd + t * kBM, kBM * 4, full);
         }
       }
     } else if (warp == kMmaWarp) {
       // ---------------------------------------------------------- MMA issuer
       if (lane == 0) {
-        const uint32_t k_addr = sb + L::kK, v_addr = sb + L::kV, ds_addr = sb + L::kDS;
-        auto stage_addr = [&](int j) { return sb + L::kStage0 + (j % kStages) * L::kStageBytes; };
-        // S^T_j = K Q_j^T (A = K, B = Q_j, both K-major)
+        // Shared-memory descriptors are built once: a K step or a stage only adds a constant to
+        // the 14-bit start-address field (every address here is below 256 KB, so it never
+        // carries). Per-MMA descriptor arithmetic would otherwise cost the single issuing thread
+        // more time than an N <= 128 MMA takes to execute.
+        const uint64_t d_qk = make_sdesc_sw128(sb + L::kStage0, 16, 1024);           // Q / dO as K-major B
+        const uint64_t d_qmn = make_sdesc_sw128(sb + L::kStage0, L::kChunkQ, 1024);  // Q / dO as MN-major B
+        const uint64_t d_v = make_sdesc_sw128(sb + L::kV, 16, 1024);                 // V as K-major A
+        const uint64_t d_kmn = make_sdesc_sw128(sb + L::kK, L::kChunkKV, 1024);      // K as MN-major A
+        const uint64_t d_ds = make_sdesc_sw128(sb + L::kDS, 8192, 1024);             // dS^T tiles as MN-major B
+        const uint32_t t_s = tmem_base + kTmS, t_dp = tmem_base + kTmDP, t_dv = tmem_base + kTmDV;
+        const uint32_t t_dk = tmem_base + kTmDK, t_k = tmem_base + kTmK, t_dq = tmem_base + kTmDQ;
+        constexpr uint32_t kStageU = L::kStageBytes >> 4, kTileQU = L::kTileQ >> 4, kDSU = L::kDSBytes >> 4;
+        // K-major K step kk: +32 bytes inside a 64-element chunk, chunks kChunkQ / kChunkKV apart
+        auto kmaj_q = [](int kk) -> uint32_t { return (uint32_t)(((kk >> 2) * L::kChunkQ + (kk & 3) * 32) >> 4); };
+        auto kmaj_kv = [](int kk) -> uint32_t { return (uint32_t)(((kk >> 2) * L::kChunkKV + (kk & 3) * 32) >> 4); };
+        // S^T_j = K Q_j^T: A = K (TMEM, packed pairs along d), B = Q_j (K-major)
         auto issue_s = [&](int j) {
-          const uint32_t q_addr = stage_addr(j) + L::kStQ;
+          const uint64_t b = d_qk + (uint64_t)((j % kStages) * kStageU);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            mma_f16_ss(tmem_base + kTmS + (j & 1) * 64,
-                       make_sdesc_sw128(k_addr + (kk >> 2) * L::kChunkKV + (kk & 3) * 32, 16, 1024),
-                       make_sdesc_sw128(q_addr + (kk >> 2) * L::kChunkQ + (kk & 3) * 32, 16, 1024), kIdescS,
-                       kk > 0 ? 1u : 0u);
-          mma_commit(bar_sfull + 8 * (j & 1));
+          for (int kk = 0; kk < D / 16; ++kk) mma_f16_ts(t_s, t_k + kk * 8, b + kmaj_q(kk), kIdescS, kk > 0 ? 1u : 0u);
+          mma_commit(bar_sfull);
         };
-        // dP^T_j = V dO_j^T
+        // dP^T_j = V dO_j^T: A = V (K-major smem), B = dO_j (K-major)
         auto issue_dp = [&](int j) {
-          const uint32_t do_addr = stage_addr(j) + L::kStDO;
+          const uint64_t b = d_qk + (uint64_t)((j % kStages) * kStageU + kTileQU);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            mma_f16_ss(tmem_base + kTmDP,
-                       make_sdesc_sw128(v_addr + (kk >> 2) * L::kChunkKV + (kk & 3) * 32, 16, 1024),
-                       make_sdesc_sw128(do_addr + (kk >> 2) * L::kChunkQ + (kk & 3) * 32, 16, 1024), kIdescS,
-                       kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) mma_f16_ss(t_dp, d_v + kmaj_kv(kk), b + kmaj_q(kk), kIdescS, kk > 0 ? 1u : 0u);
           mma_commit(bar_dpfull);
         };
-        bool ok = wait_bounded(bar_kv, 0, abort_flag, p.status, kStatusTimeoutMma);
+        bool ok = wait_bounded(bar_kvtm, 0, abort_flag, p.status, kStatusTimeoutMma);
+        if (ok) ok = wait_bounded(bar_kv, 0, abort_flag, p.status, kStatusTimeoutMma);
         if (ok) ok = wait_bounded(bar_full, 0, abort_flag, p.status, kStatusTimeoutMma);
         if (ok) {
           tc_fence_after();
@@ -333,46 +339,48 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_dp(0);
         }
         for (int j = 0; j < n_steps && ok; ++j) {
-          const uint32_t st_addr = stage_addr(j);
-          if (j + 1 < n_steps) {
+          const uint64_t st_mn = d_qmn + (uint64_t)((j % kStages) * kStageU);  // Q_j (MN-major); dO_j at + kTileQU
+          const uint32_t ph = j & 1;
+          const uint32_t acc0 = j > 0 ? 1u : 0u;
+          // P^T and dS^T are packed: the 16 columns of query group g sit at + 32 g
+          // dV += P^T_j dO_j: B = dO_j as [q][d] (MN-major), 16 rows (2048 bytes) per K step
+          ok = wait_bounded(bar_pfull, ph, abort_flag, p.status, kStatusTimeoutMma);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kBM / 16; ++kk)
+            mma_f16_ts(t_dv, t_s + (kk >> 1) * 32 + (kk & 1) * 8, st_mn + kTileQU + kk * 128, kIdescKV,
+                       kk > 0 ? 1u : acc0);
+          const bool next = j + 1 < n_steps;
+          if (next) {
             ok = wait_bounded(bar_full + 8 * ((j + 1) % kStages), ((j + 1) / kStages) & 1, abort_flag, p.status,
                               kStatusTimeoutMma);
             if (!ok) break;
             tc_fence_after();
-            issue_s(j + 1);
+            issue_s(j + 1);  // after dV_j in issue order, so P^T_j has been read
           }
-          // dV += P^T_j dO_j: A = P^T (TMEM), B = dO_j as [q][d] (MN-major)
-          ok = wait_bounded(bar_pfull + 8 * (j & 1), (j >> 1) & 1, abort_flag, p.status, kStatusTimeoutMma);
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < kBM / 16; ++kk)
-            mma_f16_ts(tmem_base + kTmDV, tmem_base + kTmS + (j & 1) * 64 + kk * 8,
-                       make_sdesc_sw128(st_addr + L::kStDO + kk * 16 * 128, L::kChunkQ, 1024), kIdescKV,
-                       (j > 0 || kk > 0) ? 1u : 0u);
           // dK += dS^T_j Q_j
-          ok = wait_bounded(bar_dsfull, j & 1, abort_flag, p.status, kStatusTimeoutMma);
+          ok = wait_bounded(bar_dsfull, ph, abort_flag, p.status, kStatusTimeoutMma);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < kBM / 16; ++kk)
-            mma_f16_ts(tmem_base + kTmDK, tmem_base + kTmDP + kk * 8,
-                       make_sdesc_sw128(st_addr + L::kStQ + kk * 16 * 128, L::kChunkQ, 1024), kIdescKV,
-                       (j > 0 || kk > 0) ? 1u : 0u);
-          // dQ^T_j = K^T dS^T_j: A = K as [key][d] (MN-major over d; for D = 64 the second
-          // 64-row chunk reads V and lands in TMEM lanes nobody reads), B = dS^T [key][q]
+            mma_f16_ts(t_dk, t_dp + (kk >> 1) * 32 + (kk & 1) * 8, st_mn + kk * 128, kIdescKV, kk > 0 ? 1u : acc0);
+          mma_commit(bar_empty + 8 * (j % kStages));  // Q_j, dO_j, -lse_j, -delta_j no longer needed
+          if (next) issue_dp(j + 1);                  // after dK_j in issue order, so dS^T_j has been read
+          // dQ^T_j = K^T dS^T_j: A = K as [key][d] (MN-major over d; for D = 64 the second 64-row
+          // chunk reads V and lands in TMEM lanes nobody reads), B = dS^T tile j & 1 [key][q]
           if (j > 0) {
-            ok = wait_bounded(bar_dqempty, (j - 1) & 1, abort_flag, p.status, kStatusTimeoutMma);
+            ok = wait_bounded(bar_dqempty, ph ^ 1, abort_flag, p.status, kStatusTimeoutMma);
             if (!ok) break;
             tc_fence_after();
           }
+          const uint64_t b_ds = d_ds + (uint64_t)((j & 1) * kDSU);
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk)
-            mma_f16_ss(tmem_base + kTmDQ, make_sdesc_sw128(k_addr + kk * 16 * 128, L::kChunkKV, 1024),
-                       make_sdesc_sw128(ds_addr + kk * 16 * 128, 8192, 1024), kIdescQ, kk > 0 ? 1u : 0u);
+            mma_f16_ss(t_dq, d_kmn + kk * 128, b_ds + kk * 128, kIdescQ, kk > 0 ? 1u : 0u);
           mma_commit(bar_dqfull);
-          mma_commit(bar_empty + 8 * (j % kStages));
-          if (j + 1 < n_steps) issue_dp(j + 1);
+          mma_commit(bar_dsfree + 8 * (j & 1));
         }
         if (ok) mma_commit(bar_final);
         if (*abort_flag) {
@@ -381,46 +389,68 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp < 4) {
+  } else if (warp < kDrainWarp0) {
     setmaxnreg_inc<kRegsCompute>();
-    // ------------------------------------------------------------ P and dS (one key row per thread)
-    const int r = warp * 32 + lane;
+    // ------------------------------------------------------------ compute (key row x 32 query columns)
+    const int quarter = warp & 3;
+    const int cg = warp >> 2;  // query columns 32 cg .. 32 cg + 31; warps of cg 0 copy K into TMEM
+    const int r = quarter * 32 + lane;
     const int kj = n0 + r;
     const bool row_valid = kj < len_k;
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_off = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t tm_row = tmem_base + lane_off;
     const uint64_t k2 = f2pack(p.scale_log2, p.scale_log2);
-    bool ok = true;
-    for (int j = 0; j < n_steps; ++j) {
+    bool ok = cg ? true : wait_bounded(bar_kv, 0, abort_flag, p.status, kStatusTimeoutSoftmax);
+    if (ok && cg == 0) {
+      // row r of K from the swizzled smem tile into TMEM as bf16/f16 pairs along d
+      const uint8_t* src = sgen + L::kK + r * 128;
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        uint32_t w[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 x = *reinterpret_cast<const uint4*>(src + c * L::kChunkKV + ((i ^ (r & 7)) << 4));
+          w[4 * i] = x.x;
+          w[4 * i + 1] = x.y;
+          w[4 * i + 2] = x.z;
+          w[4 * i + 3] = x.w;
+        }
+        tmem_st32(tm_row + kTmK + c * 32, w);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_kvtm);
+    }
+    for (int j = 0; j < n_steps && ok; ++j) {
+      const uint32_t ph = j & 1;
       const int jb = jb_lo + j % nq;
       const int hh = j / nq;
-      const int q0 = jb * kBM;
-      const uint8_t* stage = sgen + L::kStage0 + (j % kStages) * L::kStageBytes;
-      const float2* nl2 = reinterpret_cast<const float2*>(stage + L::kStNL);
-      const float2* nd2 = reinterpret_cast<const float2*>(stage + L::kStND);
+      const int q0 = jb * kBM + cg * 32;  // first query of this warp's columns
+      const float2* nl2 = reinterpret_cast<const float2*>(sgen + L::kRow + (j % kStages) * 512) + cg * 16;
+      const float2* nd2 = reinterpret_cast<const float2*>(sgen + L::kRow + (j % kStages) * 512 + 256) + cg * 16;
       // the stage's -lse / -delta rows were written by the bulk copy: observe its barrier
-      // here too (it completed long ago; stage j + 3 cannot refill it before dS_j is done)
-      if (!wait_bounded(bar_sfull + 8 * (j & 1), (j >> 1) & 1, abort_flag, p.status, kStatusTimeoutSoftmax) ||
+      // here too (it completed before S^T_j; the stage is refilled only after dS_j)
+      if (!wait_bounded(bar_sfull, ph, abort_flag, p.status, kStatusTimeoutSoftmax) ||
           !wait_bounded(bar_full + 8 * (j % kStages), (j / kStages) & 1, abort_flag, p.status,
                         kStatusTimeoutSoftmax)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float pv[kBM];  // S^T row, then P^T row
+      float pv[32];  // S^T row, then P^T row
       {
-        uint32_t su[kBM];
-        tmem_ld32p(tm_row + kTmS + (j & 1) * 64, su);
-        tmem_ld32p(tm_row + kTmS + (j & 1) * 64 + 32, su + 32);
+        uint32_t su[32];
+        tmem_ld32p(tm_row + kTmS + cg * 32, su);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < kBM; ++c) pv[c] = __uint_as_float(su[c]);
+        for (int c = 0; c < 32; ++c) pv[c] = __uint_as_float(su[c]);
       }
-      float gsc[EXTRA ? kBM : 1];  // softcap derivative
+      float gsc[EXTRA ? 32 : 1];  // softcap derivative
       if constexpr (EXTRA) {
         const int h = hk * p.group + hh;
 #pragma unroll
-        for (int c = 0; c < kBM; ++c) {
+        for (int c = 0; c < 32; ++c) {
           const int qi = q0 + c;
           float x = pv[c] * p.scale;
           if (p.bias_mode != GKO_BIAS_NONE && row_valid && qi < len_q) x += bias_at(p, zb, h, qi, kj);
@@ -440,81 +470,89 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < kBM; c += 2) {
+        for (int c = 0; c < 32; c += 2) {
           const float2 nlp = nl2[c >> 1];
-          float a, b;
-          f2unpack(fma2(f2pack(pv[c], pv[c + 1]), k2, f2pack(nlp.x, nlp.y)), a, b);
+          float a, bb;
+          f2unpack(fma2(f2pack(pv[c], pv[c + 1]), k2, f2pack(nlp.x, nlp.y)), a, bb);
           pv[c] = fast_exp2(a);
-          pv[c + 1] = fast_exp2(b);
+          pv[c + 1] = fast_exp2(bb);
         }
         // keys past the end, and (causal) queries before the key, get P = 0
-        const int lim = row_valid ? (p.causal ? kj - q0 : 0) : kBM;
+        const int lim = row_valid ? (p.causal ? kj - q0 : 0) : 32;
         if (lim > 0) {
 #pragma unroll
-          for (int c = 0; c < kBM; ++c) pv[c] = (c < lim) ? 0.f : pv[c];
+          for (int c = 0; c < 32; ++c) pv[c] = (c < lim) ? 0.f : pv[c];
         }
       }
       {
-        uint32_t pk[32];
+        uint32_t pk[16];
 #pragma unroll
-        for (int c = 0; c < 32; ++c) pk[c] = Cvt<T>::pack(pv[2 * c], pv[2 * c + 1]);
-        tmem_st32(tm_row + kTmS + (j & 1) * 64, pk);
+        for (int c = 0; c < 16; ++c) pk[c] = Cvt<T>::pack(pv[2 * c], pv[2 * c + 1]);
+        tmem_st16(tm_row + kTmS + cg * 32, pk);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar_pfull + 8 * (j & 1));
+        if (lane == 0) mbar_arrive(bar_pfull);
       }
       // dS^T = P^T (dP^T - delta)
-      if (!wait_bounded(bar_dpfull, j & 1, abort_flag, p.status, kStatusTimeoutSoftmax)) {
+      if (!wait_bounded(bar_dpfull, ph, abort_flag, p.status, kStatusTimeoutSoftmax)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t dsu[kBM];
-      tmem_ld32p(tm_row + kTmDP, dsu);
-      tmem_ld32p(tm_row + kTmDP + 32, dsu + 32);
+      uint32_t dsu[32];
+      tmem_ld32p(tm_row + kTmDP + cg * 32, dsu);
       tmem_wait_ld();
-      uint32_t pk[32];
+      uint32_t pk[16];
 #pragma unroll
-      for (int c = 0; c < kBM; c += 2) {
+      for (int c = 0; c < 32; c += 2) {
         const float2 ndp = nd2[c >> 1];
         const uint64_t t = add2(f2pack(__uint_as_float(dsu[c]), __uint_as_float(dsu[c + 1])), f2pack(ndp.x, ndp.y));
-        float a, b;
-        f2unpack(mul2(f2pack(pv[c], pv[c + 1]), t), a, b);
+        float a, bb;
+        f2unpack(mul2(f2pack(pv[c], pv[c + 1]), t), a, bb);
         if constexpr (EXTRA) {
           a *= gsc[c];
-          b *= gsc[c + 1];
+          bb *= gsc[c + 1];
         }
-        pk[c >> 1] = Cvt<T>::pack(a, b);
+        pk[c >> 1] = Cvt<T>::pack(a, bb);
       }
-      tmem_st32(tm_row + kTmDP, pk);
-      // dS^T row r into the [128 keys][64 q] tile: 16-byte chunk i at (i ^ (r & 7))
-      const uint32_t ds_row = sb + L::kDS + r * 128;
+      tmem_st16(tm_row + kTmDP + cg * 32, pk);
+      // dS^T row r into smem tile j & 1 ([128 keys][64 q], 16-byte chunk i at (i ^ (r & 7))),
+      // once dQ^T_{j-2} has finished reading that tile
+      if (j >= 2 &&
+          !wait_bounded(bar_dsfree + 8 * (j & 1), ((j - 2) >> 1) & 1, abort_flag, p.status, kStatusTimeoutSoftmax)) {
+        ok = false;
+        break;
+      }
+      const uint32_t ds_row = sb + L::kDS + (j & 1) * L::kDSBytes + r * 128;
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        st_shared_v4(ds_row + ((i ^ (r & 7)) << 4), pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      for (int i = 0; i < 4; ++i) {
+        const int ci = cg * 4 + i;
+        st_shared_v4(ds_row + ((ci ^ (r & 7)) << 4), pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      }
       fence_proxy_async_smem();
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_dsfull);
     }
-    // ------------------------------------------------------------ dk = scale * dK
+    // ------------------------------------------------------------ dk = scale * dK (columns cg * D/2 ..)
     if (ok) ok = wait_bounded(bar_final, 0, abort_flag, p.status, kStatusTimeoutSoftmax);
     if (ok) {
       tc_fence_after();
       T* row = dk_base + (int64_t)kj * p.dk_ss;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < D / 64; ++c) {
+        const int col = cg * (D / 2) + c * 32;
         uint32_t v[32];
-        tmem_ld32(tm_row + kTmDK + c * 32, v);
+        tmem_ld32(tm_row + kTmDK + col, v);
         tmem_wait_ld();
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e)
           w[e] = Cvt<T>::pack(__uint_as_float(v[2 * e]) * p.scale, __uint_as_float(v[2 * e + 1]) * p.scale);
         if (row_valid) {
-          uint4* dst = reinterpret_cast<uint4*>(row + c * 32);
+          uint4* dst = reinterpret_cast<uint4*>(row + col);
 #pragma unroll
           for (int e = 0; e < 4; ++e) dst[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
         }
@@ -524,11 +562,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     setmaxnreg_dec<kRegsDrain>();
     // ------------------------------------------------------------ dQ^T drain (one head-dim row per thread)
-    const int wq = warp - 4;
+    const int wq = warp - kDrainWarp0;
     const int dr = wq * 32 + lane;  // TMEM lane: dQ^T row d, later dV row (key)
     const uint32_t lane_off = static_cast<uint32_t>(wq * 32) << 16;
     const uint32_t tm_row = tmem_base + lane_off;
-    const bool issuer = (threadIdx.x == 128);
     bool ok = true;
     for (int j = 0; j < n_steps; ++j) {
       if (!wait_bounded(bar_dqfull, j & 1, abort_flag, p.status, kStatusTimeoutEpilogue)) {
@@ -543,39 +580,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_dqempty);
-      float* dst = p.dq_acc + tile_of(j / nq, jb_lo + j % nq) * (kBM * D);
+      if (dr < D) {
+        // accumulator block: row-major [64 queries][D]; a warp's 32 rows d are 128 contiguous bytes
+        float* dst = p.dq_acc + tile_of(j / nq, jb_lo + j % nq) * (kBM * D) + dr;
 #pragma unroll
-      for (int half = 0; half < 2 && ok; ++half) {
-        const uint32_t buf = sb + L::kDQ + half * L::kDQHalf;
-        if (issuer) {
-          bulk_wait_group_read<1>();  // this buffer's previous reduction has read it
-          mbar_arrive(bar_free + 8 * half);
-        }
-        if (!wait_bounded(bar_free + 8 * half, j & 1, abort_flag, p.status, kStatusTimeoutEpilogue)) {
-          ok = false;
-          break;
-        }
-        if (dr < D) {
-          const uint32_t row = buf + dr * 128;
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            st_shared_v4(row + ((i ^ (dr & 7)) << 4), v[half * 32 + 4 * i], v[half * 32 + 4 * i + 1],
-                         v[half * 32 + 4 * i + 2], v[half * 32 + 4 * i + 3]);
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(bar_written + 8 * half);
-        if (issuer) {
-          if (!wait_bounded(bar_written + 8 * half, j & 1, abort_flag, p.status, kStatusTimeoutEpilogue)) {
-            ok = false;
-            break;
-          }
-          bulk_reduce_add_f32(dst + half * 32 * D, buf, L::kDQHalf);
-          bulk_commit_group();
-        }
+        for (int q = 0; q < kBM; ++q) atomicAdd(dst + q * D, __uint_as_float(v[q]));
       }
-      if (!ok) break;
     }
-    if (issuer) bulk_wait_group<0>();
     // ------------------------------------------------------------ dv = dV
     if (ok) ok = wait_bounded(bar_final, 0, abort_flag, p.status, kStatusTimeoutEpilogue);
     if (ok) {
@@ -674,8 +685,9 @@ __global__ void __launch_bounds__(256) fmha_bwd_prep_kernel(const RowParams p) {
 }
 
 // ------------------------------------------------------------------ convert: dq = scale * accumulator
+// One CTA per 64-query block: 256 threads, each converting 8-element chunks of rows.
 template <typename T, int D, bool VARLEN>
-__global__ void __launch_bounds__(64) fmha_bwd_dq_kernel(const RowParams p) {
+__global__ void __launch_bounds__(256) fmha_bwd_dq_kernel(const RowParams p) {
   const int bh = (int)blockIdx.y + (int)blockIdx.z * (int)gridDim.y;
   if (bh >= p.zh) return;
   const int h = bh % p.hq;
@@ -690,28 +702,26 @@ __global__ void __launch_bounds__(64) fmha_bwd_dq_kernel(const RowParams p) {
   }
   if (jb * kBM >= len_q) return;
   const int64_t tile = (VARLEN ? (int64_t)h : (int64_t)bh) * p.tiles_per_head + base + jb;
-  const int half = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qi = jb * kBM + half * 32 + lane;
-  const float* src = p.dq_acc + tile * (kBM * D) + half * 32 * D;
-  T* dst;
-  if constexpr (VARLEN)
-    dst = reinterpret_cast<T*>(p.dq) + (int64_t)(row_q0 + qi) * p.dq_ss + (int64_t)h * p.dq_sh;
-  else
-    dst = reinterpret_cast<T*>(p.dq) + (int64_t)zb * p.dq_sz + (int64_t)h * p.dq_sh + (int64_t)qi * p.dq_ss;
-  const int sw = lane >> 2, lo = lane & 3;
-#pragma unroll 4
-  for (int d0 = 0; d0 < D; d0 += 8) {
-    uint32_t w[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int da = d0 + 2 * e, db = da + 1;
-      const float a = src[da * 32 + (((sw ^ (da & 7)) << 2) | lo)] * p.scale;
-      const float b = src[db * 32 + (((sw ^ (db & 7)) << 2) | lo)] * p.scale;
-      w[e] = Cvt<T>::pack(a, b);
-    }
-    if (qi < len_q) *reinterpret_cast<uint4*>(dst + d0) = make_uint4(w[0], w[1], w[2], w[3]);
+  const float* src = p.dq_acc + tile * (kBM * D);
+  constexpr int kChunks = kBM * D / 8;
+  for (int i = threadIdx.x; i < kChunks; i += 256) {
+    const int q = i / (D / 8), c = i % (D / 8);
+    const int qi = jb * kBM + q;
+    if (qi >= len_q) continue;
+    const float4 a = *reinterpret_cast<const float4*>(src + q * D + c * 8);
+    const float4 b = *reinterpret_cast<const float4*>(src + q * D + c * 8 + 4);
+    T* dst;
+    if constexpr (VARLEN)
+      dst = reinterpret_cast<T*>(p.dq) + (int64_t)(row_q0 + qi) * p.dq_ss + (int64_t)h * p.dq_sh;
+    else
+      dst = reinterpret_cast<T*>(p.dq) + (int64_t)zb * p.dq_sz + (int64_t)h * p.dq_sh + (int64_t)qi * p.dq_ss;
+    const float s = p.scale;
+    *reinterpret_cast<uint4*>(dst + c * 8) =
+        make_uint4(Cvt<T>::pack(a.x * s, a.y * s), Cvt<T>::pack(a.z * s, a.w * s), Cvt<T>::pack(b.x * s, b.y * s),
+                   Cvt<T>::pack(b.z * s, b.w * s));
   }
 }
+
 
 // ------------------------------------------------------------------ host side
 dim3 grid_of(int x, int64_t yz) {
@@ -759,7 +769,7 @@ int run_all(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
     if (rc) return rc;
   }
   if (q_blocks > 0) {
-    fmha_bwd_dq_kernel<T, D, VARLEN><<<rgrid, 64, 0, s>>>(rp);
+    fmha_bwd_dq_kernel<T, D, VARLEN><<<rgrid, 256, 0, s>>>(rp);
     return host::cuda_check(cudaGetLastError(), "fmha bwd dq launch");
   }
   return GKO_OK;
