@@ -43,6 +43,8 @@ PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
 TRAFFIC_FILE = REPO / "profiles" / "traffic.txt"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 METRIC = "fused-kernel TFLOP/s"
+# --small: the attention workloads at B=4, H=16 (inputs still > L2), for full ncu captures
+SMALL = False
 
 
 # --------------------------------------------------------------------------- helpers
@@ -288,7 +290,7 @@ class FmhaCausal(SwigluMLP):
         from evocompile_b200 import ops
 
         self.ops = ops
-        B, S, H, D = 8, 4096, 32, 128
+        B, S, H, D = (4, 4096, 16, 128) if SMALL else (8, 4096, 32, 128)
         h = H // world  # heads sharded
         self.B, self.S, self.H, self.D = B, S, h, D
         g = torch.Generator(device=dev).manual_seed(3000 + rank)
@@ -297,7 +299,7 @@ class FmhaCausal(SwigluMLP):
         self.q, self.k, self.v = (t.transpose(1, 2) for t in (self.qs, self.ks, self.vs))
         self.flop_gateup = self.flop_step = 4.0 * B * h * S * S * D / 2
         self.launches_per_step = 1
-        self.config = {"workload": f"fmha causal bf16 B=8 H=32 S=4096 D=128 [B,S,H,D]; {h} heads per GPU",
+        self.config = {"workload": f"fmha causal bf16 B={B} H={H} S=4096 D=128 [B,S,H,D]; {h} heads per GPU",
                        "parallelism": f"heads/{world}", "l2": "q,k,v 0.8 GB > L2"}
 
     def step(self, ev=None):
@@ -336,6 +338,77 @@ class FmhaCausal(SwigluMLP):
         q, k, v = (t[:1, :4].float().cpu() for t in (self.q, self.k, self.v))
         return (lambda: oracle.attention(q, k, v, None, self.D ** -0.5, 1)), 4.0 * 4 * self.S * self.S * self.D / 2, \
             "1 batch x 4 heads of the causal attention (fp32 oracle)"
+
+
+class FmhaBackward(SwigluMLP):
+    """Attention backward (gko::fused_sdpa_bwd) of the causal B=8 H=32 S=4096 D=128 configuration:
+    one step = the prep, main and dq-convert kernels from the saved out / lse and a random dO."""
+    name = "fmha_bwd"
+    dominant = "fmha_bwd"
+    compile_comparator = False
+
+    def __init__(self, dev, world, rank):
+        from evocompile_b200 import ops
+
+        self.ops = ops
+        B, S, H, D = (4, 4096, 16, 128) if SMALL else (8, 4096, 32, 128)
+        h = H // world  # heads sharded
+        self.B, self.S, self.H, self.D = B, S, h, D
+        g = torch.Generator(device=dev).manual_seed(4000 + rank)
+        mk = lambda: torch.randn(B, S, h, D, device=dev, generator=g).to(torch.bfloat16)  # noqa: E731
+        self.qs, self.ks, self.vs, self.dos = mk(), mk(), mk(), mk()
+        self.q, self.k, self.v, self.do = (t.transpose(1, 2) for t in (self.qs, self.ks, self.vs, self.dos))
+        if dev.type == "cuda":
+            self.out, self.lse = ops.fmha_fwd(self.q, self.k, self.v, None, D ** -0.5, 1)
+        self.flop_gateup = self.flop_step = 2.5 * 4.0 * B * h * S * S * D / 2
+        self.launches_per_step = 3
+        self.config = {"workload": f"fmha backward causal bf16 B={B} H={H} S=4096 D=128 [B,S,H,D]; {h} heads per GPU; "
+                                   "step = prep + main + dq-convert kernels (dq, dk, dv from q, k, v, out, lse, dO)",
+                       "flop": "2.5 x the forward's causal FLOP (5 GEMMs of S^2 D / 2 per head)",
+                       "parallelism": f"heads/{world}", "l2": "q,k,v,out,dO 1.3 GB > L2"}
+
+    def step(self, ev=None):
+        if ev is not None:
+            ev[0].record()
+        g = self.ops.fmha_bwd(self.q, self.k, self.v, None, self.out, self.lse, self.do, self.D ** -0.5, 1)
+        if ev is not None:
+            ev[1].record()
+        return g
+
+    def e2e_setup(self):
+        from evocompile_b200.kernels import fused_sdpa
+
+        fused_sdpa.register()
+        self.out_bshd = self.out.transpose(1, 2).contiguous()
+        dense = (self.qs, self.ks, self.vs, self.out_bshd, self.dos)
+        self.host = [t.cpu().pin_memory() for t in dense] + [self.lse.cpu().pin_memory()]
+        self.dev = [torch.empty_like(t) for t in dense] + [torch.empty_like(self.lse)]
+        self.grads_host = [torch.empty(self.B, self.H, self.S, self.D, dtype=torch.bfloat16).pin_memory()
+                           for _ in range(3)]
+        return sum(t.numel() * t.element_size() for t in self.host), sum(t.numel() * 2 for t in self.grads_host)
+
+    def e2e_step(self):
+        for d, h in zip(self.dev, self.host):
+            d.copy_(h, non_blocking=True)
+        q, k, v, o, do = (t.transpose(1, 2) for t in self.dev[:5])
+        grads = torch.ops.gko.fused_sdpa_bwd(q, k, v, q.new_empty((0,)), o, self.dev[5], do, self.D ** -0.5, 1, 0, 0.0)
+        for gh, gd in zip(self.grads_host, grads):
+            gh.copy_(gd, non_blocking=True)
+
+    def torch_reference(self):
+        import torch.nn.functional as F
+
+        q, k, v = (t.detach().requires_grad_(True) for t in (self.q, self.k, self.v))
+        o = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        do = self.do
+        return (lambda: torch.autograd.grad(o, (q, k, v), do, retain_graph=True)), ()
+
+    def cpu_sample(self):
+        import oracle
+
+        q, k, v, do = (t[:1, :1].float().cpu() for t in (self.q, self.k, self.v, self.do))
+        return (lambda: oracle.attention_bwd(q, k, v, do, None, self.D ** -0.5, 1)), \
+            2.5 * 4.0 * self.S * self.S * self.D / 2, "1 batch x 1 head of the causal attention backward (fp32 oracle, autograd)"
 
 
 class FmhaVarlen(SwigluMLP):
@@ -502,7 +575,7 @@ class TPBlockWorkload(SwigluMLP):
             "one 512-token sequence through the full-width block (fp32 oracle)"
 
 
-WORKLOADS = {c.name: c for c in (SwigluMLP, AddmmGelu, FmhaCausal, FmhaVarlen, TPBlockWorkload)}
+WORKLOADS = {c.name: c for c in (SwigluMLP, AddmmGelu, FmhaCausal, FmhaBackward, FmhaVarlen, TPBlockWorkload)}
 
 
 # --------------------------------------------------------------------------- arms
@@ -609,11 +682,12 @@ def run_ours(args):
         arms = {}
         if fn is not None:
             arms["torch_eager"] = lambda: fn(*fargs)
-            try:
-                cfn = torch.compile(fn)
-                arms["torch_compile"] = lambda: cfn(*fargs)
-            except Exception as e:  # noqa: BLE001
-                comparators["torch_compile"] = {"error": repr(e)[:200]}
+            if getattr(wl, "compile_comparator", True):
+                try:
+                    cfn = torch.compile(fn)
+                    arms["torch_compile"] = lambda: cfn(*fargs)
+                except Exception as e:  # noqa: BLE001
+                    comparators["torch_compile"] = {"error": repr(e)[:200]}
         arms["gko_repeat"] = lambda: wl.step()
         best = {}
         for name, f in list(arms.items()):
@@ -690,7 +764,11 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="swiglu")
     ap.add_argument("--no-compare", action="store_true", help="skip the torch eager / torch.compile comparators")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--small", action="store_true",
+                    help="attention workloads at B=4, H=16 (a capture-sized case for ncu --set full)")
     args = ap.parse_args()
+    global SMALL
+    SMALL = args.small
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -7,6 +7,8 @@ on the CPU, where they take their eager paths:
   silu_mul     torch.ops.gko.silu_mul  -> _eager              (eval/kernels/silu_mul.py:29-30)
   attention    fused_sdpa.fused_attention -> _fallback (F.sdpa + masks)      (eval/kernels/fused_sdpa.py:508-532)
                cutlass_sdpa.cutlass_attention (window bias, softcap)        (eval/kernels/cutlass_sdpa.py:35-136)
+  attention    torch.ops.gko.fused_sdpa with its registered autograd: on the CPU the
+  backward    _backward recomputes through _fallback and autograd (eval/kernels/fused_sdpa.py:873-898)
 
 Inputs are drawn from seeded generators and rounded to bfloat16 (stored as
 bf16) so the GPU kernels can consume them exactly; outputs are the reference's
@@ -93,6 +95,23 @@ def main(ref_root: str) -> None:
     out = cutlass_sdpa.cutlass_attention(q.float(), k.float(), v.float(), None, 0.5, 0, 0, 5.0)
     cases["attn_softcap"] = {"inputs": {"q": q, "k": k, "v": v}, "out": out.float(),
                              "args": {"scale": 0.5, "causal": 0, "softcap": 5.0}}
+
+    # --- attention backward: dq, dk, dv of <out, dO> through the reference's catalog op
+    fused_sdpa._ensure_op()
+    for causal, bias_kind in ((0, None), (1, None), (0, "keypad")):
+        q, k, v = qkv(2, 2, 40, 64)
+        do = _bf(g, 2, 2, 40, 64)
+        bias = torch.empty(0)
+        if bias_kind == "keypad":
+            bias = torch.zeros(2, 40)
+            bias[0, -7:] = torch.finfo(torch.float32).min
+        qf, kf, vf = (t.float().requires_grad_(True) for t in (q, k, v))
+        out = torch.ops.gko.fused_sdpa(qf, kf, vf, bias, 0.125, causal)
+        dq, dk, dv = torch.autograd.grad(out, (qf, kf, vf), do.float())
+        name = f"attn_bwd_c{causal}" + (f"_{bias_kind}" if bias_kind else "")
+        cases[name] = {"inputs": {"q": q, "k": k, "v": v, "dout": do, "bias": bias},
+                       "out": out.detach().float(), "dq": dq.float(), "dk": dk.float(), "dv": dv.float(),
+                       "args": {"scale": 0.125, "causal": causal}}
 
     meta = {"generator": "tests/golden/make_golden.py", "torch": torch.__version__,
             "reference": "EvoCompile eval/kernels (CPU eager paths)"}

@@ -77,3 +77,38 @@ def test_oracle_lse_matches_logsumexp():
     _, lse = oracle.attention(q, k, v, None, 0.3, 0)
     ref = torch.logsumexp(torch.matmul(q, k.transpose(-1, -2)) * 0.3, dim=-1).reshape(2, 16)
     assert torch.allclose(lse, ref, atol=1e-5)
+
+
+@pytest.mark.parametrize("name", [n for n in GOLDEN if n.startswith("attn_bwd")])
+def test_attention_bwd_golden(name):
+    """The oracle's backward (autograd of its fp32 restatement) against dq, dk, dv from the
+    reference's gko::fused_sdpa autograd on the CPU."""
+    c = GOLDEN[name]
+    i, a = c["inputs"], c["args"]
+    dq, dk, dv = oracle.attention_bwd(i["q"], i["k"], i["v"], i["dout"], i["bias"], a["scale"], a["causal"])
+    _close(dq, c["dq"], 2e-5)
+    _close(dk, c["dk"], 2e-5)
+    _close(dv, c["dv"], 2e-5)
+
+
+def test_oracle_bwd_matches_finite_differences():
+    """dL/dx of L = <attention(q, k, v), dO> by central differences in float64 (GQA, causal, softcap)."""
+    g = torch.Generator().manual_seed(7)
+    q = torch.randn(1, 4, 9, 16, generator=g, dtype=torch.float64)
+    k = torch.randn(1, 2, 11, 16, generator=g, dtype=torch.float64)
+    v = torch.randn(1, 2, 11, 16, generator=g, dtype=torch.float64)
+    do = torch.randn(1, 4, 9, 16, generator=g, dtype=torch.float64)
+    dq, dk, dv = oracle.attention_bwd(q, k, v, do, None, 0.3, 1, 0, 2.0)
+
+    def loss(q_, k_, v_):
+        return float((oracle.attention(q_, k_, v_, None, 0.3, 1, 0, 2.0)[0].double() * do).sum())
+
+    eps = 1e-3
+    for t, grad, idx in ((q, dq, (0, 3, 5, 7)), (k, dk, (0, 1, 4, 2)), (v, dv, (0, 0, 2, 9))):
+        tp, tm = t.clone(), t.clone()
+        tp[idx] += eps
+        tm[idx] -= eps
+        args_p = [tp if x is t else x for x in (q, k, v)]
+        args_m = [tm if x is t else x for x in (q, k, v)]
+        fd = (loss(*args_p) - loss(*args_m)) / (2 * eps)
+        assert abs(fd - float(grad[idx])) <= 1e-3 * max(1.0, abs(fd)), (fd, float(grad[idx]))
