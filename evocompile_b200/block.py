@@ -124,8 +124,8 @@ class TPBlock:
         q = qkv[:, : hq * hd].view(T, hq, hd)
         k = qkv[:, hq * hd: (hq + hkv) * hd].view(T, hkv, hd)
         v = qkv[:, (hq + hkv) * hd:].view(T, hkv, hd)
-        ops.rope_(q, cfg.rope_theta, seq_len=S)
-        ops.rope_(k, cfg.rope_theta, seq_len=S)
+        # q and k heads are adjacent in each qkv row: one RoPE launch covers both
+        ops.rope_(qkv[:, : (hq + hkv) * hd].view(T, hq + hkv, hd), cfg.rope_theta, seq_len=S)
         as4 = lambda t: t.view(B, S, t.shape[1], hd).transpose(1, 2)     # noqa: E731  [B, H, S, D] views
         attn = torch.empty(T, hq, hd, device=x.device, dtype=x.dtype)
         ops.fmha_fwd(as4(q), as4(k), as4(v), None, hd ** -0.5, 1, out=as4(attn))

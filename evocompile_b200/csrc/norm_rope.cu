@@ -55,28 +55,40 @@ struct Vec8<__half> {
 constexpr int kNormThreads = 256;
 constexpr int kMaxVecPerThread = 8;  // cols <= 256 * 8 * 8 = 16384
 
-// One CTA per row. The row (x + r) stays in registers between the two passes.
-template <typename T>
+// One CTA per row; VPT 16-byte vectors per thread, chosen on the host as the smallest
+// power of two covering the row, so short rows keep few registers and many rows in flight.
+// The row (x + r) stays in registers between the two passes.
+template <typename T, int VPT>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ r,
                                                                const T* __restrict__ w, T* __restrict__ y,
                                                                T* __restrict__ sum_out, int cols, int64_t ld,
                                                                float eps) {
   const int64_t row = blockIdx.x;
   const int nvec = cols / 8;
-  float v[kMaxVecPerThread][8];
+  float v[VPT][8];
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxVecPerThread; ++i) {
+  for (int i = 0; i < VPT; ++i) {
     const int vi = threadIdx.x + i * kNormThreads;
-    if (vi < nvec) {
-      Vec8<T>::load(x + row * ld + vi * 8, v[i]);
-      if (r) {
+    if (vi < nvec) Vec8<T>::load(x + row * ld + vi * 8, v[i]);
+  }
+  if (r) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = threadIdx.x + i * kNormThreads;
+      if (vi < nvec) {
         float rr[8];
         Vec8<T>::load(r + row * ld + vi * 8, rr);
 #pragma unroll
         for (int e = 0; e < 8; ++e) v[i][e] += rr[e];
+        if (sum_out) Vec8<T>::store(sum_out + row * ld + vi * 8, v[i]);
       }
-      if (sum_out) Vec8<T>::store(sum_out + row * ld + vi * 8, v[i]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * kNormThreads;
+    if (vi < nvec) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) ss = fmaf(v[i][e], v[i][e], ss);
     }
@@ -91,7 +103,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const T* __restri
   for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
   const float inv = rsqrtf(tot / (float)cols + eps);
 #pragma unroll
-  for (int i = 0; i < kMaxVecPerThread; ++i) {
+  for (int i = 0; i < VPT; ++i) {
     const int vi = threadIdx.x + i * kNormThreads;
     if (vi < nvec) {
       float ww[8];
@@ -105,35 +117,66 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const T* __restri
 
 // Rotate-half RoPE (the Llama / HF convention): for pair (i, i + D/2) of a head,
 //   out_i = x_i cos(p f_i) - x_{i+D/2} sin(p f_i),  out_{i+D/2} = x_{i+D/2} cos(p f_i) + x_i sin(p f_i),
-// f_i = theta^(-2i/D), p = token position. One thread per (token, head, i < D/2).
+// f_i = theta^(-2i/D), p = token position. One thread per (token, 8 consecutive i): it evaluates
+// its 8 angles once and applies them to every head of the token with 16-byte loads and stores
+// (the 8 threads of a token cover a head's two 128-byte halves).
 template <typename T>
 __global__ void __launch_bounds__(256) rope_kernel(T* __restrict__ x, int64_t tokens, int heads, int d,
                                                    int64_t st_token, int64_t st_head,
                                                    const int* __restrict__ pos, int seq_len,
                                                    float log2_theta) {
   const int half = d / 2;
-  const int64_t n = tokens * heads * half;
+  const int chunks = half / 8;
+  const int64_t n = tokens * chunks;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < n;
        idx += (int64_t)gridDim.x * blockDim.x) {
-    const int i = (int)(idx % half);
-    const int64_t th = idx / half;
-    const int h = (int)(th % heads);
-    const int64_t t = th / heads;
+    const int i0 = (int)(idx % chunks) * 8;
+    const int64_t t = idx / chunks;
     const int p = pos ? pos[t] : (int)(t % seq_len);
-    const float inv_freq = exp2f(-log2_theta * (2.f * (float)i / (float)d));
-    float s, c;
-    sincosf((float)p * inv_freq, &s, &c);
-    T* base = x + t * st_token + (int64_t)h * st_head;
-    const float a = static_cast<float>(base[i]);
-    const float b = static_cast<float>(base[i + half]);
-    base[i] = static_cast<T>(a * c - b * s);
-    base[i + half] = static_cast<T>(b * c + a * s);
+    float c[8], s[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float inv_freq = exp2f(-log2_theta * (2.f * (float)(i0 + e) / (float)d));
+      sincosf((float)p * inv_freq, &s[e], &c[e]);
+    }
+    T* row = x + t * st_token + i0;
+    for (int h = 0; h < heads; ++h) {
+      T* base = row + (int64_t)h * st_head;
+      float a[8], b[8];
+      Vec8<T>::load(base, a);
+      Vec8<T>::load(base + half, b);
+      float oa[8], ob[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        oa[e] = a[e] * c[e] - b[e] * s[e];
+        ob[e] = b[e] * c[e] + a[e] * s[e];
+      }
+      Vec8<T>::store(base, oa);
+      Vec8<T>::store(base + half, ob);
+    }
   }
 }
 
 }  // namespace
 
 using gko::host::fail;
+
+namespace {
+template <typename T>
+void launch_rmsnorm(int vpt, int64_t rows, const void* x, const void* r, const void* w, void* y, void* sum_out,
+                    int cols, int64_t ld, float eps, cudaStream_t s) {
+  const T* xp = static_cast<const T*>(x);
+  const T* rp = static_cast<const T*>(r);
+  const T* wp = static_cast<const T*>(w);
+  T* yp = static_cast<T*>(y);
+  T* sp = static_cast<T*>(sum_out);
+  const unsigned g = (unsigned)rows;
+  if (vpt == 1) rmsnorm_kernel<T, 1><<<g, kNormThreads, 0, s>>>(xp, rp, wp, yp, sp, cols, ld, eps);
+  else if (vpt == 2) rmsnorm_kernel<T, 2><<<g, kNormThreads, 0, s>>>(xp, rp, wp, yp, sp, cols, ld, eps);
+  else if (vpt == 4) rmsnorm_kernel<T, 4><<<g, kNormThreads, 0, s>>>(xp, rp, wp, yp, sp, cols, ld, eps);
+  else rmsnorm_kernel<T, 8><<<g, kNormThreads, 0, s>>>(xp, rp, wp, yp, sp, cols, ld, eps);
+}
+}  // namespace
 
 extern "C" int gko_rmsnorm(int dtype, int64_t rows, int64_t cols, const void* x, const void* residual,
                            const void* weight, float eps, void* out, void* sum_out, int64_t ld,
@@ -151,15 +194,12 @@ extern "C" int gko_rmsnorm(int dtype, int64_t rows, int64_t cols, const void* x,
     return fail(GKO_ERR_UNSUPPORTED, "rmsnorm needs 16-byte aligned buffers");
   if (rows > 0x7fffffffll) return fail(GKO_ERR_UNSUPPORTED, "too many rows");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t per = (cols / 8 + kNormThreads - 1) / kNormThreads;  // vectors per thread
+  const int vpt = per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : 8;
   if (dtype == GKO_BF16)
-    rmsnorm_kernel<__nv_bfloat16><<<(unsigned)rows, kNormThreads, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(residual),
-        static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out),
-        static_cast<__nv_bfloat16*>(sum_out), (int)cols, ld, eps);
+    launch_rmsnorm<__nv_bfloat16>(vpt, rows, x, residual, weight, out, sum_out, (int)cols, ld, eps, s);
   else
-    rmsnorm_kernel<__half><<<(unsigned)rows, kNormThreads, 0, s>>>(
-        static_cast<const __half*>(x), static_cast<const __half*>(residual), static_cast<const __half*>(weight),
-        static_cast<__half*>(out), static_cast<__half*>(sum_out), (int)cols, ld, eps);
+    launch_rmsnorm<__half>(vpt, rows, x, residual, weight, out, sum_out, (int)cols, ld, eps, s);
   return gko::host::cuda_check(cudaGetLastError(), "rmsnorm launch");
 }
 
@@ -173,7 +213,10 @@ extern "C" int gko_rope(int dtype, int64_t tokens, int64_t heads, int64_t head_d
   if (!x) return fail(GKO_ERR_INVALID, "null pointer argument");
   if (!positions && seq_len <= 0) return fail(GKO_ERR_INVALID, "rope needs positions or seq_len > 0");
   if (!(theta > 1.f)) return fail(GKO_ERR_INVALID, "rope theta must be > 1");
-  const int64_t n = tokens * heads * (head_dim / 2);
+  if (head_dim % 16 || st_token % 8 || st_head % 8 || !gko::host::aligned16(x))
+    return fail(GKO_ERR_UNSUPPORTED, "rope needs head_dim a multiple of 16, token/head strides multiples of 8 "
+                                     "elements and a 16-byte aligned buffer");
+  const int64_t n = tokens * (head_dim / 16);
   int64_t blocks = (n + 255) / 256;
   const int64_t cap = (int64_t)gko::host::sm_count() * 16;
   if (blocks > cap) blocks = cap;
