@@ -45,6 +45,9 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 METRIC = "fused-kernel TFLOP/s"
 # --small: the attention workloads at B=4, H=16 (inputs still > L2), for full ncu captures
 SMALL = False
+# --tp-comm: how the tensor-parallel block sums its row-parallel outputs ("fused": inside the
+# GEMM over NVLink; "nccl": GEMM then NCCL all-reduce)
+TP_COMM = "fused"
 
 
 # --------------------------------------------------------------------------- helpers
@@ -495,7 +498,7 @@ class TPBlockWorkload(SwigluMLP):
             import torch.distributed as dist
 
             group = dist.group.WORLD
-        self.block = TPBlock(shard_weights(full, self.cfg, rank, world), self.cfg, group)
+        self.block = TPBlock(shard_weights(full, self.cfg, rank, world), self.cfg, group, comm=TP_COMM)
         if world > 1:
             del full
             torch.cuda.empty_cache()
@@ -505,14 +508,16 @@ class TPBlockWorkload(SwigluMLP):
         self.flop_step = self.cfg.flops(T, self.S)
         ff_l = self.cfg.d_ff // world
         self.flop_gateup = 2.0 * T * self.cfg.d_model * 2 * ff_l
-        self.launches_per_step = 9  # rmsnorm, qkv gemm, rope x2, fmha, o gemm, rmsnorm, gate/up, down
+        self.launches_per_step = 8  # rmsnorm, qkv gemm, rope, fmha, o gemm, rmsnorm, gate/up, down
         self.config = {
             "workload": "llama3-70b block prefill bf16: d_model 8192, 64 q / 8 kv heads, D 128, d_ff 28672, "
                         "B=4 S=4096; RMSNorm -> QKV -> RoPE(5e5) -> causal GQA FMHA -> o-proj -> residual -> "
                         "RMSNorm -> SwiGLU -> down -> residual",
             "model": "Llama-3-70B block (synthetic random-init weights N(0,0.02), x ~ N(0,1))",
             "global_batch": self.B, "seq_len": self.S, "tokens": T,
-            "parallelism": f"tp{world} (column-parallel QKV / gate-up, row-parallel o / down, NCCL all-reduce)",
+            "parallelism": f"tp{world} (column-parallel QKV / gate-up, row-parallel o / down; row-parallel sums: "
+                           + ("none" if world == 1 else "inside the GEMM over NVLink (multicast reduction)"
+                              if TP_COMM == "fused" else "NCCL all-reduce") + ")",
             "l2": "weights 1.7 GB / tp, activations > L2; no flush",
         }
 
@@ -766,9 +771,12 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--small", action="store_true",
                     help="attention workloads at B=4, H=16 (a capture-sized case for ncu --set full)")
+    ap.add_argument("--tp-comm", choices=("fused", "nccl"), default="fused",
+                    help="tp_block: sum row-parallel outputs inside the GEMM (fused) or with NCCL")
     args = ap.parse_args()
-    global SMALL
+    global SMALL, TP_COMM
     SMALL = args.small
+    TP_COMM = args.tp_comm
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -11,7 +11,11 @@ row-parallel outputs are summed with an NCCL all-reduce. RMSNorm weights are rep
 
 Every GEMM is the tcgen05 kernel (the SwiGLU one fused), attention the tcgen05 FMHA reading
 q/k/v in place from the QKV output and writing [tokens, heads, d] for the o-projection,
-RMSNorm (+ residual add) and RoPE are the library's memory-bound kernels.
+RMSNorm (+ residual add) and RoPE are the library's memory-bound kernels. With
+``comm="fused"`` (the default for more than one rank) the two row-parallel projections
+reduce their outputs across the group inside the GEMM over NVLink
+(``evocompile_b200.tp.FusedAllReduceLinear``); ``comm="nccl"`` runs the GEMM and then an
+NCCL all-reduce.
 """
 
 from __future__ import annotations
@@ -100,16 +104,32 @@ class TPBlock:
     """One rank of the tensor-parallel block. ``group`` is a torch.distributed process group
     (NCCL) or None for a single GPU."""
 
-    def __init__(self, local: dict, cfg: BlockConfig, group=None):
+    def __init__(self, local: dict, cfg: BlockConfig, group=None, comm: str = "fused"):
+        if comm not in ("fused", "nccl"):
+            raise ValueError(f"comm must be 'fused' or 'nccl', got {comm!r}")
         self.w = local
         self.cfg = cfg
         self.group = group
         self.world = 1 if group is None else torch.distributed.get_world_size(group)
+        self.comm = comm
+        self._fused = {}
 
-    def _all_reduce(self, t):
-        if self.world > 1:
-            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.SUM, group=self.group)
-        return t
+    def _row_parallel(self, x, weight, slot):
+        """x @ weight^T summed over the group (row-parallel projection)."""
+        if self.world == 1:
+            return ops.linear(x, weight)
+        if self.comm == "nccl":
+            y = ops.linear(x, weight)
+            torch.distributed.all_reduce(y, op=torch.distributed.ReduceOp.SUM, group=self.group)
+            return y
+        from .tp import FusedAllReduceLinear
+
+        key = (slot, x.shape[0], weight.shape[0], x.dtype)
+        f = self._fused.get(key)
+        if f is None:  # collective: every rank builds it at the same call
+            f = FusedAllReduceLinear(x.shape[0], weight.shape[0], x.dtype, x.device, self.group)
+            self._fused[key] = f
+        return f(x, weight)
 
     def forward(self, x: torch.Tensor, events=None) -> torch.Tensor:
         """x [B, S, d_model] (bf16) -> [B, S, d_model]. ``events`` (start, end) CUDA events, if
@@ -129,12 +149,12 @@ class TPBlock:
         as4 = lambda t: t.view(B, S, t.shape[1], hd).transpose(1, 2)     # noqa: E731  [B, H, S, D] views
         attn = torch.empty(T, hq, hd, device=x.device, dtype=x.dtype)
         ops.fmha_fwd(as4(q), as4(k), as4(v), None, hd ** -0.5, 1, out=as4(attn))
-        o = self._all_reduce(ops.linear(attn.view(T, hq * hd), w["wo"]))  # row-parallel partial -> sum
+        o = self._row_parallel(attn.view(T, hq * hd), w["wo"], 0)          # row-parallel partial -> sum
         h2, x1 = ops.rmsnorm(o, w["mlp_norm"], cfg.eps, residual=x2, return_sum=True)
         if events is not None:
             events[0].record()
         g = ops.linear_swiglu(h2, w["w_gate_up"])                        # [T, ff_local]
         if events is not None:
             events[1].record()
-        dn = self._all_reduce(ops.linear(g, w["w_down"]))
+        dn = self._row_parallel(g, w["w_down"], 1)
         return (x1 + dn).view(B, S, d)

@@ -81,6 +81,7 @@ int dispatch_tc(int epi, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb
                 const CUtensorMap& td, const GemmParams& p, cudaStream_t s) {
   if (!b_mn) {
     switch (epi) {
+      case kEpiAllReduce: return launch_tc<T, kEpiAllReduce, false>(ta, tb, td, p, s);
       case kEpiNone: return launch_tc<T, kEpiNone, false>(ta, tb, td, p, s);
       case kEpiGelu: return launch_tc<T, kEpiGelu, false>(ta, tb, td, p, s);
       case kEpiRelu: return launch_tc<T, kEpiRelu, false>(ta, tb, td, p, s);
@@ -101,7 +102,8 @@ int dispatch_tc(int epi, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb
 int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_total,
            int64_t up_offset, const void* a, int64_t lda, const void* b, int64_t ldb, bool b_mn,
            const void* bias, int bias_kind, void* d, int64_t ldd, unsigned* status,
-           cudaStream_t stream) {
+           cudaStream_t stream, void* red_mc = nullptr, void* const* red_peers = nullptr,
+           int red_world = 0) {
   if (!host::aligned16(a) || !host::aligned16(b) || !host::aligned16(d))
     return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs 16-byte aligned operand bases");
   if (lda % 8 || ldb % 8 || ldd % 8)
@@ -152,7 +154,7 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
 #ifndef GKO_GEMM_PAIR_MIN_M
 #define GKO_GEMM_PAIR_MIN_M 0x7fffffff
 #endif
-  const bool pair = M >= GKO_GEMM_PAIR_MIN_M;
+  const bool pair = M >= GKO_GEMM_PAIR_MIN_M && epi != kEpiAllReduce;
   const int block_m = pair ? 2 * gemm::kBM : gemm::kBM;
   p.m_blocks = (int)((M + block_m - 1) / block_m);
   const int bn = gemm::block_n_out(epi);
@@ -189,6 +191,10 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
   p.bias = bias;
   p.bias_kind = bias_kind;
   p.status = status;
+  p.red_mc = red_mc;
+  p.red_peers = red_peers;
+  p.red_world = red_world;
+  p.red_ld = ldd;
   if (p.num_tiles == 0) return GKO_OK;
   if (pair) {
     if (dtype == GKO_BF16) return dispatch_pair<__nv_bfloat16>(epi, b_mn, ta, tb, td, p, stream);
@@ -291,4 +297,24 @@ extern "C" int gko_linear_swiglu(int dtype, int64_t m, int64_t h, int64_t k, con
     return run_tc(dtype, kEpiSwiglu, m, h, k, 2 * h, h, x, x_sm, w, w_sk, true, nullptr,
                   kBiasNone, out, ldo, status, s);
   return fail(GKO_ERR_UNSUPPORTED, "tensor-core SwiGLU needs a weight with unit stride in one dim");
+}
+
+extern "C" int gko_linear_allreduce(int dtype, int64_t m, int64_t n, int64_t k, const void* x, int64_t x_sm,
+                                    int64_t x_sk, const void* w, int64_t w_sn, int64_t w_sk, void* out,
+                                    int64_t ldo, void* out_multicast, void* const* out_peers, int world,
+                                    unsigned int* status, void* stream) {
+  if (dtype != GKO_BF16 && dtype != GKO_F16)
+    return fail(GKO_ERR_UNSUPPORTED, "linear_allreduce takes bf16 or f16 (dtype code %d)", dtype);
+  if (m < 0 || n < 0 || k < 0 || world < 1) return fail(GKO_ERR_INVALID, "negative size or world < 1");
+  if (m == 0 || n == 0) return GKO_OK;
+  if (!out || !x || !w) return fail(GKO_ERR_INVALID, "null operand pointer");
+  if (!out_multicast && !out_peers)
+    return fail(GKO_ERR_INVALID, "linear_allreduce needs a multicast address or the peers' output pointers");
+  if (out_multicast && !host::aligned16(out_multicast))
+    return fail(GKO_ERR_UNSUPPORTED, "linear_allreduce needs a 16-byte aligned multicast address");
+  if (k == 0) return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs k > 0");
+  if (x_sk != 1 || w_sk != 1)
+    return fail(GKO_ERR_UNSUPPORTED, "linear_allreduce needs row-major x [m, k] and weight [n, k]");
+  return run_tc(dtype, kEpiAllReduce, m, n, k, n, 0, x, x_sm, w, w_sn, false, nullptr, kBiasNone, out, ldo, status,
+                reinterpret_cast<cudaStream_t>(stream), out_multicast, out_peers, world);
 }

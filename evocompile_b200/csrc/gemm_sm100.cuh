@@ -8,6 +8,10 @@
 //   kEpiGelu   : D = gelu_erf(A*B^T + bias)              gko::addmm_gelu
 //   kEpiRelu   : D = relu(A*B^T + bias)
 //   kEpiSwiglu : D = silu(A*Bg^T) * (A*Bu^T)             gko::gemm_swiglu, B = [Bg; Bu]
+//   kEpiAllReduce: D_r += A*B^T on every rank r of a tensor-parallel group (row-parallel
+//                linear + all-reduce in one kernel): each staged output chunk is added into
+//                all ranks' D through the NVLink multicast address (in-switch reduction),
+//                or through each peer's mapped D when no multicast object exists
 //
 // CTA = 10 warps: warp 0 TMA producer, warp 1 MMA issuer (+TMEM owner),
 //                 warps 2..9 epilogue (TMEM -> registers -> smem -> TMA store); two
@@ -25,7 +29,7 @@
 
 namespace gko {
 
-enum : int { kEpiNone = 0, kEpiGelu = 1, kEpiRelu = 2, kEpiSwiglu = 3 };
+enum : int { kEpiNone = 0, kEpiGelu = 1, kEpiRelu = 2, kEpiSwiglu = 3, kEpiAllReduce = 4 };
 enum : int { kBiasNone = 0, kBiasF16 = 1, kBiasBF16 = 2, kBiasF32 = 3 };
 
 struct GemmParams {
@@ -42,6 +46,12 @@ struct GemmParams {
   const void* bias;
   int bias_kind;
   unsigned* status;
+  // kEpiAllReduce: destination D of every rank, by multicast address (red_mc) or, without
+  // one, by the device array of the ranks' mapped D pointers (red_peers, red_world entries)
+  void* red_mc;
+  void* const* red_peers;
+  int red_world;
+  int64_t red_ld;  // row stride of D in elements
 };
 
 namespace gemm {
@@ -157,11 +167,32 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
       __syncwarp();
       if (lane == 0) release();
     }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d_hint(tm_d, buf, col_base + c * 64, row0, l2_policy_evict_first());
-      bulk_commit_group();
+    if constexpr (EPI == kEpiAllReduce) {
+      // row-contiguous read-back of the staged [32 rows x 64 columns]: 8 lanes per row, so a
+      // warp instruction adds four 128-byte row segments
+      __syncwarp();
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int r = it * 4 + (lane >> 3), j = lane & 7;
+        const uint4 v = ld_shared_v4(buf + r * 128 + ((j ^ (r & 7)) << 4));
+        const int grow = row0 + r, gcol = col_base + c * 64 + j * 8;
+        if (grow < p.M && gcol < p.N_out) {
+          const int64_t off = ((int64_t)grow * p.red_ld + gcol) * (int64_t)sizeof(T);
+          if (p.red_mc) {
+            multimem_red_add_x8<T>(static_cast<uint8_t*>(p.red_mc) + off, v);
+          } else {
+            for (int w = 0; w < p.red_world; ++w) red_add_x8<T>(static_cast<uint8_t*>(p.red_peers[w]) + off, v);
+          }
+        }
+      }
+      __syncwarp();
+    } else {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d_hint(tm_d, buf, col_base + c * 64, row0, l2_policy_evict_first());
+        bulk_commit_group();
+      }
     }
   }
 }
@@ -345,6 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                             [&] { mbar_arrive(bar_tempty + 8 * acc); });
     }
     if (lane == 0) bulk_wait_group<0>();
+    // cross-GPU reductions are performed at system scope before the kernel is seen as done
+    if constexpr (EPI == kEpiAllReduce) __threadfence_system();
     __syncwarp();
   }
 

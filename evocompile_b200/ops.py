@@ -440,3 +440,37 @@ def fmha_varlen_bwd(q, k, v, out, lse, dout, cu_seqlens_q, cu_seqlens_k, max_seq
             )
         _lib.check(rc, "gko_fmha_varlen_bwd")
     return dq, dk, dv
+
+
+# --------------------------------------------------------------------------- tensor-parallel GEMM + all-reduce
+def linear_allreduce(x, weight, out, multicast_ptr: int, peers_dev_ptr: int, world: int):
+    """out of every rank += x @ weight^T, inside the GEMM (see evocompile_b200.tp).
+
+    ``out`` is this rank's copy of a symmetric-memory buffer, already zeroed on every rank;
+    ``multicast_ptr`` its NVLink multicast address (0 if none) and ``peers_dev_ptr`` the device
+    array of all ranks' copies. The caller orders the zeroing and the completion with group
+    barriers.
+    """
+    dev = _lib.require_cuda(x, weight, out)
+    if x.dim() != 2 or weight.dim() != 2 or out.dim() != 2:
+        raise RuntimeError("linear_allreduce: x [m, k], weight [n, k], out [m, n]")
+    if x.dtype != weight.dtype or x.dtype != out.dtype:
+        raise RuntimeError("linear_allreduce: x, weight, out dtypes differ")
+    m, k = x.shape
+    n = weight.shape[0]
+    if weight.shape[1] != k or tuple(out.shape) != (m, n):
+        raise RuntimeError(f"linear_allreduce: shape mismatch x {tuple(x.shape)} weight {tuple(weight.shape)} "
+                           f"out {tuple(out.shape)}")
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    if weight.stride(1) != 1:
+        weight = weight.contiguous()
+    if m and n:
+        with torch.cuda.device(dev):
+            rc = _lib.load().gko_linear_allreduce(
+                _lib.dtype_code(x.dtype), m, n, k, _ptr(x), x.stride(0), 1, _ptr(weight), weight.stride(0), 1,
+                _ptr(out), out.stride(0), ctypes.c_void_p(multicast_ptr or 0), ctypes.c_void_p(peers_dev_ptr or 0),
+                int(world), _status_ptr(dev), _stream(dev),
+            )
+        _lib.check(rc, "gko_linear_allreduce")
+    return out

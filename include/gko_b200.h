@@ -227,6 +227,25 @@ int gko_fmha_varlen_bwd(int dtype, int64_t b, int64_t hq, int64_t hkv, int64_t d
                         int64_t workspace_bytes, unsigned int* status, void* stream);
 
 /*
+ * Row-parallel linear with the tensor-parallel all-reduce inside the GEMM:
+ * out_r += x @ w^T on every rank r of the group, where x is this rank's [m, k] input
+ * slice (row stride x_sm, x_sk == 1) and w its [n, k] weight slice (row stride w_sn,
+ * w_sk == 1). The epilogue adds each finished bf16/f16 output chunk into every rank's out
+ * (row stride ldo): through `out_multicast`, an NVLink multicast address bound to all
+ * ranks' out buffers (one in-switch reduction), or, when that is NULL, through
+ * `out_peers`, a device array of the `world` ranks' mapped out pointers (one reduction
+ * per rank). Every rank's out must be zero before any rank starts and the caller waits
+ * for all ranks to finish before reading (group barriers around the call).
+ *
+ * No reference counterpart (the reference has no tensor-parallel path); it replaces the
+ * GEMM + NCCL all-reduce pair of the Llama-3-70B block's o- and down-projections.
+ */
+int gko_linear_allreduce(int dtype, int64_t m, int64_t n, int64_t k, const void* x, int64_t x_sm,
+                         int64_t x_sk, const void* w, int64_t w_sn, int64_t w_sk, void* out,
+                         int64_t ldo, void* out_multicast, void* const* out_peers, int world,
+                         unsigned int* status, void* stream);
+
+/*
  * out[i] = silu(x[i]) * y[i] over n contiguous elements (dtype f16, bf16 or f32).
  *
  * Replaces the Triton launch _triton (eval/kernels/silu_mul.py:33-43) behind
