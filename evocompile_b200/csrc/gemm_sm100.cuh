@@ -310,6 +310,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
+      // Descriptors are built once: a stage or a K step only adds a constant to the 14-bit
+      // start-address field (shared-memory addresses stay below 256 KB, so it never carries);
+      // building them per MMA costs the issuing thread more than an MMA's execution time.
+      const uint64_t d_a0 = make_sdesc_sw128(sA, 16, 1024);
+      const uint64_t d_b0 = B_MN ? make_sdesc_sw128(sB, kBBytes / 4, 1024) : make_sdesc_sw128(sB, 16, 1024);
+      constexpr uint32_t kKStepB = B_MN ? (16 * 128) >> 4 : 32 >> 4;  // per K16 step, 16-byte units
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
@@ -327,18 +333,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = sA + stage * kABytes;
-          const uint32_t b_addr = sB + stage * kBBytes;
+          const uint64_t a_st = d_a0 + (uint64_t)(stage * (kABytes >> 4));
+          const uint64_t b_st = d_b0 + (uint64_t)(stage * (kBBytes >> 4));
+          const uint32_t acc0 = kb != 0 ? 1u : 0u;
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t adesc = make_sdesc_sw128(a_addr + kk * 32, 16, 1024);
-            uint64_t bdesc;
-            if constexpr (!B_MN)
-              bdesc = make_sdesc_sw128(b_addr + kk * 32, 16, 1024);
-            else
-              bdesc = make_sdesc_sw128(b_addr + kk * 16 * 128, kBBytes / 4, 1024);
-            mma_f16_ss(d_tmem, adesc, bdesc, kIdesc, (kb | kk) != 0);
-          }
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_f16_ss(d_tmem, a_st + kk * (32 >> 4), b_st + kk * kKStepB, kIdesc, kk > 0 ? 1u : acc0);
           mma_commit(bar_empty + 8 * stage);
           if (++stage == kStages) {
             stage = 0;
