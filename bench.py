@@ -380,6 +380,85 @@ class FmhaBackward(SwigluMLP):
             2.5 * 4.0 * self.S * self.S * self.D / 2, "1 batch x 1 head of the causal attention backward (fp32 oracle, autograd)"
 
 
+class SwigluTrain(SwigluMLP):
+    """Training step of the fused gate/up SwiGLU (Llama-3-8B MLP shape): forward through
+    gko::gemm_swiglu_aux (the kernel also writes the gate/up pre-activations) and backward
+    from them (swiglu_bwd kernel, dX on the tensor-core GEMM, dW on cuBLAS) — no recomputed
+    forward GEMM. FLOP = 3 x the forward's 2 M D 2H."""
+    name = "swiglu_train"
+    dominant = "swiglu_gateup"
+    compile_comparator = False
+
+    def __init__(self, dev, world, rank):
+        super().__init__(dev, world, rank)
+        from evocompile_b200.kernels import gemm_swiglu
+
+        gemm_swiglu.register()
+        self.api = gemm_swiglu
+        self.xg = self.x.detach().clone().requires_grad_(True)
+        self.wg = self.wgu.detach().clone().requires_grad_(True)
+        g = torch.Generator(device=dev).manual_seed(1500 + rank)
+        self.dy = torch.randn(self.T, self.H, device=dev, generator=g).to(torch.bfloat16)
+        self.flop_step = 3.0 * self.flop_gateup
+        self.launches_per_step = 3  # gate/up + aux, swiglu_bwd, dX GEMM (dW runs on cuBLAS)
+        self.config = dict(self.config, workload="swiglu training step, llama3-8b shape: X[8192,4096] bf16, "
+                           "W_gate/W_up packed [28672,4096]; step = fused gate/up forward saving gate/up + "
+                           "backward (dX, dW) without recomputing the forward GEMM")
+
+    def _fwd_bwd(self, fn):
+        self.xg.grad = None
+        self.wg.grad = None
+        fn(self.xg, self.wg).backward(self.dy)
+        return self.xg.grad
+
+    def step(self, ev=None):
+        if ev is not None:
+            ev[0].record()
+        out = self._fwd_bwd(self.api.apply_train)
+        if ev is not None:
+            ev[1].record()
+        return out
+
+    def e2e_setup(self):
+        api = self.api
+        wg = self.wg
+        dy = self.dy
+
+        def train(d):
+            x = d[0].detach().requires_grad_(True)  # a leaf view; the pipeline's buffer stays grad-free
+            wg.grad = None
+            api.apply_train(x, wg).backward(dy)
+            return x.grad
+
+        return [self.x.cpu().pin_memory()], train
+
+    def torch_reference(self):
+        import torch.nn.functional as F
+
+        def eager(x, w):
+            g, u = F.linear(x, w).chunk(2, dim=-1)
+            return F.silu(g) * u
+
+        return (lambda: self._fwd_bwd(eager)), ()
+
+    def extra_arms(self):
+        return {"gko_recompute_backward": lambda: self._fwd_bwd(torch.ops.gko.gemm_swiglu)}
+
+    def cpu_sample(self):
+        import oracle
+
+        xs = self.x[:256].float().cpu().requires_grad_(True)
+        w = self.wgu.float().cpu().requires_grad_(True)
+        dy = self.dy[:256].float().cpu()
+
+        def fn():
+            xs.grad = None
+            w.grad = None
+            oracle.gemm_swiglu(xs, w).backward(dy)
+
+        return fn, 3.0 * 2.0 * 256 * self.D * 2 * self.H, "256 of 8192 tokens, forward + backward (fp32 oracle autograd)"
+
+
 class FmhaVarlen(SwigluMLP):
     name = "fmha_varlen"
     dominant = "fmha_varlen_fwd"
@@ -582,7 +661,8 @@ class E2EPipeline:
         cur.wait_stream(self.down)
 
 
-WORKLOADS = {c.name: c for c in (SwigluMLP, AddmmGelu, FmhaCausal, FmhaBackward, FmhaVarlen, TPBlockWorkload)}
+WORKLOADS = {c.name: c for c in (SwigluMLP, SwigluTrain, AddmmGelu, FmhaCausal, FmhaBackward, FmhaVarlen,
+                                  TPBlockWorkload)}
 
 
 # --------------------------------------------------------------------------- arms
@@ -700,6 +780,8 @@ def run_ours(args):
                 except Exception as e:  # noqa: BLE001
                     comparators["torch_compile"] = {"error": repr(e)[:200]}
         arms["gko_repeat"] = lambda: wl.step()
+        if hasattr(wl, "extra_arms"):
+            arms.update(wl.extra_arms())
         best = {}
         for name, f in list(arms.items()):
             try:

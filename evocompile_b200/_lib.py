@@ -76,6 +76,15 @@ SIGNATURES = {
         _int,
         [_int, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _int, _vp, _vp],
     ),
+    "gko_addmm_act_aux": (
+        _int,
+        [_int, _int, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _int, _vp, _i64, _vp, _i64, _vp, _vp],
+    ),
+    "gko_linear_swiglu_aux": (
+        _int,
+        [_int, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _vp],
+    ),
+    "gko_swiglu_bwd": (_int, [_int, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp]),
     "gko_silu_mul": (_int, [_int, _i64, _vp, _vp, _vp, _vp, _vp]),
     "gko_selftest_wait_timeout": (_int, [_vp, ctypes.c_longlong, _vp]),
     "gko_rmsnorm": (_int, [_int, _i64, _i64, _vp, _vp, _vp, _fl, _vp, _vp, _i64, _vp, _vp]),

@@ -103,9 +103,11 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
            int64_t up_offset, const void* a, int64_t lda, const void* b, int64_t ldb, bool b_mn,
            const void* bias, int bias_kind, void* d, int64_t ldd, unsigned* status,
            cudaStream_t stream, void* red_mc = nullptr, void* const* red_peers = nullptr,
-           int red_world = 0) {
-  if (!host::aligned16(a) || !host::aligned16(b) || !host::aligned16(d))
+           int red_world = 0, void* aux = nullptr, int64_t aux_ld = 0) {
+  if (!host::aligned16(a) || !host::aligned16(b) || !host::aligned16(d) || (aux && !host::aligned16(aux)))
     return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs 16-byte aligned operand bases");
+  if (aux && aux_ld % 8)
+    return fail(GKO_ERR_UNSUPPORTED, "the pre-activation output needs a row stride that is a multiple of 8");
   if (lda % 8 || ldb % 8 || ldd % 8)
     return fail(GKO_ERR_UNSUPPORTED,
                 "tensor-core GEMM needs row strides that are multiples of 8 elements "
@@ -154,7 +156,7 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
 #ifndef GKO_GEMM_PAIR_MIN_M
 #define GKO_GEMM_PAIR_MIN_M 0x7fffffff
 #endif
-  const bool pair = M >= GKO_GEMM_PAIR_MIN_M && epi != kEpiAllReduce;
+  const bool pair = M >= GKO_GEMM_PAIR_MIN_M && epi != kEpiAllReduce && !aux;
   const int block_m = pair ? 2 * gemm::kBM : gemm::kBM;
   p.m_blocks = (int)((M + block_m - 1) / block_m);
   const int bn = gemm::block_n_out(epi);
@@ -195,6 +197,8 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
   p.red_peers = red_peers;
   p.red_world = red_world;
   p.red_ld = ldd;
+  p.aux = aux;
+  p.aux_ld = aux_ld;
   if (p.num_tiles == 0) return GKO_OK;
   if (pair) {
     if (dtype == GKO_BF16) return dispatch_pair<__nv_bfloat16>(epi, b_mn, ta, tb, td, p, stream);
@@ -317,4 +321,52 @@ extern "C" int gko_linear_allreduce(int dtype, int64_t m, int64_t n, int64_t k, 
     return fail(GKO_ERR_UNSUPPORTED, "linear_allreduce needs row-major x [m, k] and weight [n, k]");
   return run_tc(dtype, kEpiAllReduce, m, n, k, n, 0, x, x_sm, w, w_sn, false, nullptr, kBiasNone, out, ldo, status,
                 reinterpret_cast<cudaStream_t>(stream), out_multicast, out_peers, world);
+}
+
+extern "C" int gko_addmm_act_aux(int dtype, int act, int64_t m, int64_t n, int64_t k, const void* a, int64_t a_sm,
+                                 int64_t a_sk, const void* b, int64_t b_sk, int64_t b_sn, const void* bias,
+                                 int bias_dtype, void* d, int64_t ldd, void* z, int64_t ldz, unsigned int* status,
+                                 void* stream) {
+  if (dtype != GKO_BF16 && dtype != GKO_F16)
+    return fail(GKO_ERR_UNSUPPORTED, "the pre-activation output is produced on the bf16 / f16 path only");
+  if (act != GKO_ACT_NONE && act != GKO_ACT_GELU && act != GKO_ACT_RELU)
+    return fail(GKO_ERR_INVALID, "unknown activation code %d", act);
+  if (m < 0 || n < 0 || k < 0) return fail(GKO_ERR_INVALID, "negative GEMM size");
+  if (m == 0 || n == 0) return GKO_OK;
+  if (!d || !z || (k && (!a || !b))) return fail(GKO_ERR_INVALID, "null operand pointer");
+  const int bk = bias_kind_of(bias, bias_dtype);
+  if (bk < 0) return fail(GKO_ERR_INVALID, "unknown bias dtype code %d", bias_dtype);
+  const int epi = act == GKO_ACT_GELU ? kEpiGelu : act == GKO_ACT_RELU ? kEpiRelu : kEpiNone;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (k == 0) return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs k > 0");
+  if (a_sk != 1)
+    return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs a row-major mat1 (stride(-1) == 1)");
+  if (b_sk == 1)
+    return run_tc(dtype, epi, m, n, k, n, 0, a, a_sm, b, b_sn, false, bias, bk, d, ldd, status, s, nullptr, nullptr,
+                  0, z, ldz);
+  if (b_sn == 1)
+    return run_tc(dtype, epi, m, n, k, n, 0, a, a_sm, b, b_sk, true, bias, bk, d, ldd, status, s, nullptr, nullptr,
+                  0, z, ldz);
+  return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs mat2 with unit stride in one dimension");
+}
+
+extern "C" int gko_linear_swiglu_aux(int dtype, int64_t m, int64_t h, int64_t k, const void* x, int64_t x_sm,
+                                     int64_t x_sk, const void* w, int64_t w_sn, int64_t w_sk, void* out, int64_t ldo,
+                                     void* gate_up, int64_t ldg, unsigned int* status, void* stream) {
+  if (dtype != GKO_BF16 && dtype != GKO_F16)
+    return fail(GKO_ERR_UNSUPPORTED, "the pre-activation output is produced on the bf16 / f16 path only");
+  if (m < 0 || h < 0 || k < 0) return fail(GKO_ERR_INVALID, "negative GEMM size");
+  if (m == 0 || h == 0) return GKO_OK;
+  if (!out || !gate_up || (k && (!x || !w))) return fail(GKO_ERR_INVALID, "null operand pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (k == 0) return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs k > 0");
+  if (x_sk != 1)
+    return fail(GKO_ERR_UNSUPPORTED, "tensor-core SwiGLU needs a row-major x (stride(-1) == 1)");
+  if (w_sk == 1)
+    return run_tc(dtype, kEpiSwiglu, m, h, k, 2 * h, h, x, x_sm, w, w_sn, false, nullptr, kBiasNone, out, ldo, status,
+                  s, nullptr, nullptr, 0, gate_up, ldg);
+  if (w_sn == 1)
+    return run_tc(dtype, kEpiSwiglu, m, h, k, 2 * h, h, x, x_sm, w, w_sk, true, nullptr, kBiasNone, out, ldo, status,
+                  s, nullptr, nullptr, 0, gate_up, ldg);
+  return fail(GKO_ERR_UNSUPPORTED, "tensor-core SwiGLU needs a weight with unit stride in one dim");
 }

@@ -52,6 +52,11 @@ struct GemmParams {
   void* const* red_peers;
   int red_world;
   int64_t red_ld;  // row stride of D in elements
+  // Optional second output for the backward (NULL: none): the pre-activation z = A*B^T + bias
+  // (kEpiNone / kEpiGelu / kEpiRelu), or [gate | up] (kEpiSwiglu: gate in columns [0, N_out),
+  // up in [N_out, 2 N_out)); row stride aux_ld elements.
+  void* aux;
+  int64_t aux_ld;
 };
 
 namespace gemm {
@@ -105,7 +110,19 @@ __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); 
 // t_row) into the output: TMEM -> registers -> epilogue math -> 128B-swizzled
 // staging buffer -> TMA store of [32 rows x 64 columns] per chunk. Calls
 // `release()` (on one lane, after the warp's last TMEM read of the tile) so the
-// MMA warp may reuse the accumulator.
+// MMA warp may reuse the accumulator. With p.aux set, each lane also writes its row's
+// pre-activation values (32 per half chunk) to the auxiliary output with 16-byte stores.
+template <typename T>
+__device__ __forceinline__ void store_aux_row(void* aux, int64_t ld, int row, int col, int M, int N,
+                                              const uint32_t (&v)[16]) {
+  if (row >= M) return;
+  T* dst = static_cast<T*>(aux) + (int64_t)row * ld + col;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if (col + 8 * j < N)
+      reinterpret_cast<uint4*>(dst)[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
 template <typename T, int EPI, typename Release>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtensorMap* tm_d,
                                               uint32_t t_row, int row0, int col_base, int half,
@@ -134,16 +151,29 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
           const float u0 = __uint_as_float(u[2 * i]), u1 = __uint_as_float(u[2 * i + 1]);
           packed[i] = Cvt<T>::pack(silu(g0) * u0, silu(g1) * u1);
         }
+        if (p.aux) {
+          uint32_t zg[16], zu[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            zg[i] = Cvt<T>::pack(__uint_as_float(g[2 * i]), __uint_as_float(g[2 * i + 1]));
+            zu[i] = Cvt<T>::pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
+          }
+          const int row = row0 + lane, col = col_base + col0;
+          store_aux_row<T>(p.aux, p.aux_ld, row, col, p.M, p.N_out, zg);
+          store_aux_row<T>(p.aux, p.aux_ld, row, p.N_out + col, p.M, 2 * p.N_out, zu);
+        }
       } else {
         uint32_t v[32];
         tmem_ld32(t_row + col0, v);
         // one bias value per lane, broadcast across the row by shuffles
         const float bl = load_bias(p.bias, p.bias_kind, col_base + col0 + lane, p.N_out);
         tmem_wait_ld();
+        uint32_t zp[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           float x0 = __uint_as_float(v[2 * i]) + __shfl_sync(0xffffffffu, bl, 2 * i);
           float x1 = __uint_as_float(v[2 * i + 1]) + __shfl_sync(0xffffffffu, bl, 2 * i + 1);
+          zp[i] = Cvt<T>::pack(x0, x1);
           if constexpr (EPI == kEpiGelu) {
             x0 = gelu_erf(x0);
             x1 = gelu_erf(x1);
@@ -153,6 +183,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
           }
           packed[i] = Cvt<T>::pack(x0, x1);
         }
+        if (p.aux) store_aux_row<T>(p.aux, p.aux_ld, row0 + lane, col_base + col0, p.M, p.N_out, zp);
       }
       // 128B-swizzled staging row: 16-byte piece j of row `lane` lives at j ^ (lane & 7).
 #pragma unroll

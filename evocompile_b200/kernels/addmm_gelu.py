@@ -10,6 +10,11 @@ Drop-in for the reference module eval/kernels/addmm_gelu.py:
   exact-fp32 kernel. Unsupported inputs raise; nothing falls back.
 * autograd recomputes the pre-activation and uses gelu_backward, as the
   reference's _addmm_gelu_backward (:175-185).
+* ``torch.ops.gko.addmm_gelu_aux(bias, mat1, mat2) -> (out, z)`` and
+  ``addmm_gelu_train(bias, mat1, mat2)`` (training form, no reference counterpart):
+  the forward kernel also writes the pre-activation z, so the backward runs
+  gelu_backward on it and the two gradient GEMMs without recomputing the forward
+  GEMM (the recompute the reference notes costs its training steps).
 * ``fuse_addmm_gelu(graph)`` rewrites gelu(addmm / F.linear / nn.Linear /
   mm + bias), with up to two view/reshape nodes in between, and the decomposed
   0.5 * x * (1 + erf(x / sqrt 2)) form, into the op (the patterns of :355-512).
@@ -17,6 +22,8 @@ Drop-in for the reference module eval/kernels/addmm_gelu.py:
 """
 
 from __future__ import annotations
+
+from typing import Tuple
 
 import torch
 
@@ -58,6 +65,31 @@ def _backward(ctx, grad_output):
     return g_bias, g_mat1, g_mat2
 
 
+def _setup_aux(ctx, inputs, output):
+    bias, mat1, mat2 = inputs
+    ctx.save_for_backward(bias, mat1, mat2, output[1])
+
+
+def _backward_aux(ctx, grad_output, grad_z):
+    bias, mat1, mat2, z = ctx.saved_tensors
+    gz = aten.gelu_backward.default(grad_output, z, approximate="none")
+    if grad_z is not None:
+        gz = gz + grad_z
+    needs = getattr(ctx, "needs_input_grad", None) or (True, True, True)
+    g2 = gz.reshape(-1, gz.shape[-1])
+    g_bias = g2.sum(0).reshape(bias.shape) if needs[0] else None
+    # dX = dZ @ mat2^T on the tensor-core GEMM (mat2^T is the row-major weight for a Linear)
+    g_mat1 = ops.addmm_act(None, g2, mat2.t(), _lib.ACT_NONE).reshape(mat1.shape) if needs[1] else None
+    g_mat2 = mat1.reshape(-1, mat1.shape[-1]).t().mm(g2) if needs[2] else None
+    return g_bias, g_mat1, g_mat2
+
+
+def addmm_gelu_train(bias, mat1, mat2):
+    """gelu(mat1 @ mat2 + bias) whose backward reuses the pre-activation saved by the forward kernel."""
+    _ensure_op()
+    return torch.ops.gko.addmm_gelu_aux(bias, mat1, mat2)[0]
+
+
 def _ensure_op():
     global _OP_READY, _AUTOGRADED
     if not _OP_READY:
@@ -70,6 +102,20 @@ def _ensure_op():
             @addmm_gelu.register_fake
             def _(bias, mat1, mat2):
                 return mat1.new_empty(tuple(mat1.shape[:-1]) + (mat2.shape[-1],))
+
+        if not (hasattr(torch.ops, "gko") and hasattr(torch.ops.gko, "addmm_gelu_aux")):
+
+            @torch.library.custom_op("gko::addmm_gelu_aux", mutates_args=())
+            def addmm_gelu_aux(bias: torch.Tensor, mat1: torch.Tensor,
+                               mat2: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+                return ops.addmm_act(bias, mat1, mat2, _lib.ACT_GELU, save_pre=True)
+
+            @addmm_gelu_aux.register_fake
+            def _(bias, mat1, mat2):
+                shape = (*mat1.shape[:-1], mat2.shape[-1])
+                return mat1.new_empty(shape), mat1.new_empty(shape)
+
+            torch.library.register_autograd("gko::addmm_gelu_aux", _backward_aux, setup_context=_setup_aux)
 
         _OP_READY = True
     if not _AUTOGRADED:

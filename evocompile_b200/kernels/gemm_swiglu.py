@@ -7,9 +7,17 @@ intermediate never reaches memory. Autograd recomputes gate/up as the
 reference's _backward (:177-200). ``apply(x, weight)`` is the public entry the
 TorchTitan FusedSwiGLU hook calls (:244-250); ``swiglu_mlp`` adds the
 down-projection on the same tensor-core GEMM.
+
+Training form (no reference counterpart): ``torch.ops.gko.gemm_swiglu_aux(x, weight)
+-> (out, gate_up)`` and ``apply_train(x, weight)``: the forward kernel also writes the
+[.., 2H] gate/up pre-activations, the backward turns them into [d_gate | d_up] with one
+elementwise kernel (gko_swiglu_bwd) and runs dX on the tensor-core GEMM, without the
+reference backward's recomputation of the gate/up GEMM.
 """
 
 from __future__ import annotations
+
+from typing import Tuple
 
 import torch
 import torch.nn.functional as F
@@ -46,6 +54,32 @@ def _backward(ctx, grad_out):
     return gx, gw
 
 
+def _setup_aux(ctx, inputs, output):
+    x, weight = inputs
+    ctx.save_for_backward(x, weight, output[1])
+
+
+def _backward_aux(ctx, grad_out, grad_gu):
+    from .. import _lib
+
+    x, weight, gate_up = ctx.saved_tensors
+    d_gu = ops.swiglu_bwd(grad_out.contiguous(), gate_up)
+    if grad_gu is not None:
+        d_gu = d_gu + grad_gu
+    needs = getattr(ctx, "needs_input_grad", None) or (True, True)
+    d2 = d_gu.reshape(-1, d_gu.shape[-1])
+    # dX = d_gate_up @ [Wg; Wu] on the tensor-core GEMM (the weight read as an MN-major operand)
+    gx = ops.addmm_act(None, d2, weight, _lib.ACT_NONE).reshape(x.shape) if needs[0] else None
+    gw = d2.t().mm(x.reshape(-1, x.shape[-1])) if needs[1] else None
+    return gx, gw
+
+
+def apply_train(x, weight):
+    """silu(x Wg^T) * (x Wu^T) whose backward reuses the gate/up values saved by the forward kernel."""
+    _ensure_op()
+    return torch.ops.gko.gemm_swiglu_aux(x, weight)[0]
+
+
 def _ensure_op():
     global _OP_READY, _AUTOGRADED
     if not _OP_READY:
@@ -58,6 +92,19 @@ def _ensure_op():
             @_op.register_fake
             def _(x, weight):
                 return x.new_empty(*x.shape[:-1], weight.shape[0] // 2)
+
+        if not (hasattr(torch.ops, "gko") and hasattr(torch.ops.gko, "gemm_swiglu_aux")):
+
+            @torch.library.custom_op("gko::gemm_swiglu_aux", mutates_args=())
+            def _aux(x: torch.Tensor, weight: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+                return ops.linear_swiglu(x, weight, save_pre=True)
+
+            @_aux.register_fake
+            def _(x, weight):
+                h = weight.shape[0] // 2
+                return x.new_empty(*x.shape[:-1], h), x.new_empty(*x.shape[:-1], 2 * h)
+
+            torch.library.register_autograd("gko::gemm_swiglu_aux", _backward_aux, setup_context=_setup_aux)
 
         _OP_READY = True
     if not _AUTOGRADED:

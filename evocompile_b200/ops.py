@@ -30,12 +30,14 @@ def _stream(dev):
 
 
 # --------------------------------------------------------------------------- GEMM
-def addmm_act(bias, mat1, mat2, act: int = _lib.ACT_GELU):
+def addmm_act(bias, mat1, mat2, act: int = _lib.ACT_GELU, save_pre: bool = False):
     """act(mat1 @ mat2 + bias) with mat1 [..., K] and mat2 [K, N].
 
     Follows the contract of gko::addmm_gelu (eval/kernels/addmm_gelu.py:150-161,
     192-210): output shape mat1.shape[:-1] + (N,), dtype of mat1. mat2 is
     usually the transposed view W^T of a Linear weight and is read in place.
+    With save_pre, returns (out, z) where z = mat1 @ mat2 + bias is written by the same
+    kernel (bf16 / f16), for a backward that needs no recomputation.
     """
     dev = _lib.require_cuda(mat1, mat2, bias)
     if mat2.dim() != 2:
@@ -72,14 +74,24 @@ def addmm_act(bias, mat1, mat2, act: int = _lib.ACT_GELU):
             bias_t = bias_t.contiguous()
         bias_dt = _lib.dtype_code(bias_t.dtype)
     out = torch.empty((M, N), device=dev, dtype=mat1.dtype)
+    z = torch.empty((M, N), device=dev, dtype=mat1.dtype) if save_pre else None
     if M and N:
         with torch.cuda.device(dev):
             a_sm = a.stride(0) if M > 1 else max(K, 8)
-            rc = _lib.load().gko_addmm_act(
-                dt, act, M, N, K, _ptr(a), a_sm, a.stride(1), _ptr(b), b.stride(0), b.stride(1),
-                _ptr(bias_t), bias_dt, _ptr(out), out.stride(0), _status_ptr(dev), _stream(dev),
-            )
-        _lib.check(rc, "gko_addmm_act")
+            if save_pre:
+                rc = _lib.load().gko_addmm_act_aux(
+                    dt, act, M, N, K, _ptr(a), a_sm, a.stride(1), _ptr(b), b.stride(0), b.stride(1),
+                    _ptr(bias_t), bias_dt, _ptr(out), out.stride(0), _ptr(z), z.stride(0), _status_ptr(dev),
+                    _stream(dev),
+                )
+            else:
+                rc = _lib.load().gko_addmm_act(
+                    dt, act, M, N, K, _ptr(a), a_sm, a.stride(1), _ptr(b), b.stride(0), b.stride(1),
+                    _ptr(bias_t), bias_dt, _ptr(out), out.stride(0), _status_ptr(dev), _stream(dev),
+                )
+        _lib.check(rc, "gko_addmm_act_aux" if save_pre else "gko_addmm_act")
+    if save_pre:
+        return out.reshape(*lead, N), z.reshape(*lead, N)
     return out.reshape(*lead, N)
 
 
@@ -88,11 +100,12 @@ def linear(x, weight, bias=None):
     return addmm_act(bias, x, weight.t(), _lib.ACT_NONE)
 
 
-def linear_swiglu(x, weight):
+def linear_swiglu(x, weight, save_pre: bool = False):
     """silu(x @ Wg.T) * (x @ Wu.T) with weight = [Wg; Wu] of shape (2H, D).
 
     Contract of gko::gemm_swiglu (eval/kernels/gemm_swiglu.py:147-169,
-    208-220): x (..., D) -> (..., H), dtype of x.
+    208-220): x (..., D) -> (..., H), dtype of x. With save_pre, returns (out, gate_up)
+    where gate_up = [x Wg^T | x Wu^T] (..., 2H) is written by the same kernel (bf16 / f16).
     """
     dev = _lib.require_cuda(x, weight)
     if weight.dim() != 2 or weight.shape[0] % 2:
@@ -113,15 +126,43 @@ def linear_swiglu(x, weight):
     if dt != _lib.F32 and not (w.stride(0) == 1 or w.stride(1) == 1):
         w = w.contiguous()
     out = torch.empty((M, H), device=dev, dtype=x.dtype)
+    gu = torch.empty((M, 2 * H), device=dev, dtype=x.dtype) if save_pre else None
     if M and H:
         with torch.cuda.device(dev):
             a_sm = a.stride(0) if M > 1 else max(D, 8)
-            rc = _lib.load().gko_linear_swiglu(
-                dt, M, H, D, _ptr(a), a_sm, a.stride(1), _ptr(w), w.stride(0), w.stride(1),
+            if save_pre:
+                rc = _lib.load().gko_linear_swiglu_aux(
+                    dt, M, H, D, _ptr(a), a_sm, a.stride(1), _ptr(w), w.stride(0), w.stride(1),
+                    _ptr(out), out.stride(0), _ptr(gu), gu.stride(0), _status_ptr(dev), _stream(dev),
+                )
+            else:
+                rc = _lib.load().gko_linear_swiglu(
+                    dt, M, H, D, _ptr(a), a_sm, a.stride(1), _ptr(w), w.stride(0), w.stride(1),
+                    _ptr(out), out.stride(0), _status_ptr(dev), _stream(dev),
+                )
+        _lib.check(rc, "gko_linear_swiglu_aux" if save_pre else "gko_linear_swiglu")
+    if save_pre:
+        return out.reshape(*lead, H), gu.reshape(*lead, 2 * H)
+    return out.reshape(*lead, H)
+
+
+def swiglu_bwd(dy, gate_up):
+    """[d_gate | d_up] of y = silu(g) * u from dy (..., H) and the saved gate_up = [g | u] (..., 2H)."""
+    dev = _lib.require_cuda(dy, gate_up)
+    H = dy.shape[-1]
+    if gate_up.shape[-1] != 2 * H or gate_up.shape[:-1] != dy.shape[:-1] or dy.dtype != gate_up.dtype:
+        raise RuntimeError(f"swiglu_bwd: dy {tuple(dy.shape)} / gate_up {tuple(gate_up.shape)} mismatch")
+    d2 = dy.reshape(-1, H).contiguous()
+    g2 = gate_up.reshape(-1, 2 * H).contiguous()
+    out = torch.empty_like(g2)
+    if d2.shape[0] and H:
+        with torch.cuda.device(dev):
+            rc = _lib.load().gko_swiglu_bwd(
+                _lib.dtype_code(dy.dtype), d2.shape[0], H, _ptr(d2), d2.stride(0), _ptr(g2), g2.stride(0),
                 _ptr(out), out.stride(0), _status_ptr(dev), _stream(dev),
             )
-        _lib.check(rc, "gko_linear_swiglu")
-    return out.reshape(*lead, H)
+        _lib.check(rc, "gko_swiglu_bwd")
+    return out.reshape(gate_up.shape)
 
 
 def swiglu_mlp(x, w_gate_up, w_down):

@@ -227,6 +227,32 @@ int gko_fmha_varlen_bwd(int dtype, int64_t b, int64_t hq, int64_t hkv, int64_t d
                         int64_t workspace_bytes, unsigned int* status, void* stream);
 
 /*
+ * Training forms of gko_addmm_act and gko_linear_swiglu that also write what the backward
+ * needs, so it recomputes no GEMM (the reference backward re-runs the forward GEMM,
+ * eval/kernels/addmm_gelu.py:175-185, eval/kernels/gemm_swiglu.py:177-200).
+ * gko_addmm_act_aux: as gko_addmm_act, plus z[m, n] (row stride ldz) = the pre-activation
+ * mat1 @ mat2 + bias. gko_linear_swiglu_aux: as gko_linear_swiglu, plus gate_up[m, 2h]
+ * (row stride ldg) = [x Wg^T | x Wu^T]. bf16 / f16 only (tensor-core path).
+ */
+int gko_addmm_act_aux(int dtype, int act, int64_t m, int64_t n, int64_t k, const void* a, int64_t a_sm,
+                      int64_t a_sk, const void* b, int64_t b_sk, int64_t b_sn, const void* bias,
+                      int bias_dtype, void* d, int64_t ldd, void* z, int64_t ldz, unsigned int* status,
+                      void* stream);
+int gko_linear_swiglu_aux(int dtype, int64_t m, int64_t h, int64_t k, const void* x, int64_t x_sm,
+                          int64_t x_sk, const void* w, int64_t w_sn, int64_t w_sk, void* out,
+                          int64_t ldo, void* gate_up, int64_t ldg, unsigned int* status, void* stream);
+
+/*
+ * SwiGLU backward from the saved pre-activations: with s = sigmoid(g) and dy[rows, h],
+ * d_gate_up[:, :h] = dy u s (1 + g (1 - s)) and d_gate_up[:, h:] = dy g s, where
+ * gate_up = [g | u] is [rows, 2h]. Row strides in elements; bf16 / f16; h and strides
+ * multiples of 8. Replaces the elementwise part of the reference backward
+ * (eval/kernels/gemm_swiglu.py:177-200).
+ */
+int gko_swiglu_bwd(int dtype, int64_t rows, int64_t h, const void* dy, int64_t ld_dy, const void* gate_up,
+                   int64_t ld_gu, void* d_gate_up, int64_t ld_dgu, unsigned int* status, void* stream);
+
+/*
  * Row-parallel linear with the tensor-parallel all-reduce inside the GEMM:
  * out_r += x @ w^T on every rank r of the group, where x is this rank's [m, k] input
  * slice (row stride x_sm, x_sk == 1) and w its [n, k] weight slice (row stride w_sn,
