@@ -16,8 +16,9 @@
 //              more than 2^8, and at the end normalises O_t and writes out / lse.
 // TMEM (512 columns): S0|P0 [0,128), S1|P1 [128,256), O0 [256,256+D), O1 [384,384+D).
 // Registers: the CTA launches with 12 x 32 threads x 168 registers; the
-// producer/MMA warpgroup (warps 8-11) drops to 56 registers per thread and the two
-// softmax warpgroups rise to 216 (2 x 128 x 216 + 128 x 56 = 62464 <= 64512).
+// producer/MMA warpgroup (warps 8-11) drops to 72 registers per thread and the two
+// softmax warpgroups rise to 216 (2 x 128 x 216 + 128 x 72 = 64512, the whole launch;
+// at 56 the MMA issuer spilled).
 // Semantics follow the reference Triton kernel _flash_fwd
 // (eval/kernels/fused_sdpa.py:25-157): logits = scale * q.k (+ bias), then
 // softcap, then masks (key padding, causal key <= query, |key - query| <= window);
@@ -38,7 +39,7 @@ constexpr int kThreads = 384;      // 2 x 4 softmax warps, producer, MMA, 2 idle
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr uint32_t kRegsSoftmax = 216;
-constexpr uint32_t kRegsControl = 56;
+constexpr uint32_t kRegsControl = 72;
 static_assert(2 * 128 * kRegsSoftmax + 128 * kRegsControl <= 384 * 168, "register split exceeds the launch");
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
