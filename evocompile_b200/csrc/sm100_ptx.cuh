@@ -180,15 +180,6 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       : "memory");
 }
 
-// Untiled bulk reduction shared -> global: dst[i] += src[i] over `bytes / 4` floats,
-// performed at L2; tracked by the bulk-group commit / wait below.
-__device__ __forceinline__ void bulk_reduce_add_f32(void* dst, uint32_t src, uint32_t bytes) {
-  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.f32 [%0], [%1], %2;" ::"l"(
-                   reinterpret_cast<uint64_t>(dst)),
-               "r"(src), "r"(bytes)
-               : "memory");
-}
-
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
