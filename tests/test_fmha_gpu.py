@@ -50,6 +50,25 @@ def test_fmha_dense(dtype, d, causal, s):
     _check(out, lse, ref_o, ref_l)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("causal", [0, 1])
+def test_fmha_growing_logits(d, causal):
+    """Key norms grow with each 128-key tile and query norms differ per row, so the row
+    maximum of later tiles exceeds the running maximum by more than the lazy-rescale
+    threshold for some rows of a warp and not for others: covers the first-half recompute,
+    the O rescale and the rows that keep their maximum."""
+    g = torch.Generator().manual_seed(77 + d + causal)
+    sq, sk = 256, 640
+    q = torch.randn(1, 2, sq, d, generator=g) * (0.1 + 2 * torch.rand(1, 2, sq, 1, generator=g))
+    grow = 1.0 + 3.0 * (torch.arange(sk) // 128).float()
+    k = torch.randn(1, 2, sk, d, generator=g) * grow.view(1, 1, sk, 1)
+    v = torch.randn(1, 2, sk, d, generator=g)
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    ref_o, ref_l = oracle.attention(q, k, v, None, d ** -0.5, causal)
+    out, lse = ops.fmha_fwd(q.cuda(), k.cuda(), v.cuda(), None, d ** -0.5, causal)
+    _check(out, lse, ref_o, ref_l)
+
+
 @pytest.mark.parametrize("sq,sk", [(64, 300), (300, 64), (129, 1000)])
 @pytest.mark.parametrize("causal", [0, 1])
 def test_fmha_cross_lengths(sq, sk, causal):
