@@ -46,8 +46,8 @@ METRIC = "fused-kernel TFLOP/s"
 # --small: the attention workloads at B=4, H=16 (inputs still > L2), for full ncu captures
 SMALL = False
 # --tp-comm: how the tensor-parallel block sums its row-parallel outputs ("fused": inside the
-# GEMM over NVLink; "nccl": GEMM then NCCL all-reduce)
-TP_COMM = "fused"
+# GEMM over NVLink; "nccl": GEMM then NCCL all-reduce; "auto": fused on two ranks, NCCL on more)
+TP_COMM = "auto"
 
 
 # --------------------------------------------------------------------------- helpers
@@ -554,7 +554,7 @@ class TPBlockWorkload(SwigluMLP):
             "global_batch": self.B, "seq_len": self.S, "tokens": T,
             "parallelism": f"tp{world} (column-parallel QKV / gate-up, row-parallel o / down; row-parallel sums: "
                            + ("none" if world == 1 else "inside the GEMM over NVLink (multicast reduction)"
-                              if TP_COMM == "fused" else "NCCL all-reduce") + ")",
+                              if self.block.comm == "fused" else "NCCL all-reduce") + ")",
             "l2": "weights 1.7 GB / tp, activations > L2; no flush",
         }
 
@@ -859,8 +859,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--small", action="store_true",
                     help="attention workloads at B=4, H=16 (a capture-sized case for ncu --set full)")
-    ap.add_argument("--tp-comm", choices=("fused", "nccl"), default="fused",
-                    help="tp_block: sum row-parallel outputs inside the GEMM (fused) or with NCCL")
+    ap.add_argument("--tp-comm", choices=("auto", "fused", "nccl"), default="auto",
+                    help="tp_block: sum row-parallel outputs inside the GEMM (fused), with NCCL, or "
+                         "fused on two ranks and NCCL on more (auto)")
     args = ap.parse_args()
     global SMALL, TP_COMM
     SMALL = args.small
