@@ -11,7 +11,8 @@ row-parallel outputs are summed with an NCCL all-reduce. RMSNorm weights are rep
 
 Every GEMM is the tcgen05 kernel (the SwiGLU one fused), attention the tcgen05 FMHA reading
 q/k/v in place from the QKV output and writing [tokens, heads, d] for the o-projection,
-RMSNorm (+ residual add) and RoPE are the library's memory-bound kernels. With
+RMSNorm (+ residual add) and RoPE are the library's memory-bound kernels; on one rank the
+closing residual add runs in the down projection's epilogue (``ops.linear_residual``). With
 ``comm="fused"`` the two row-parallel projections reduce their outputs across the group
 inside the GEMM over NVLink (``evocompile_b200.tp.FusedAllReduceLinear``); ``comm="nccl"``
 runs the GEMM and then an NCCL all-reduce. ``comm="auto"`` (the default) picks the fused
@@ -160,5 +161,7 @@ class TPBlock:
         g = ops.linear_swiglu(h2, w["w_gate_up"])                        # [T, ff_local]
         if events is not None:
             events[1].record()
+        if self.world == 1:  # down projection with the residual add in its epilogue, in place
+            return ops.linear_residual(g, w["w_down"], x1, out=x1).view(B, S, d)
         dn = self._row_parallel(g, w["w_down"], 1)
         return (x1 + dn).view(B, S, d)

@@ -103,7 +103,11 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
            int64_t up_offset, const void* a, int64_t lda, const void* b, int64_t ldb, bool b_mn,
            const void* bias, int bias_kind, void* d, int64_t ldd, unsigned* status,
            cudaStream_t stream, void* red_mc = nullptr, void* const* red_peers = nullptr,
-           int red_world = 0, void* aux = nullptr, int64_t aux_ld = 0) {
+           int red_world = 0, void* aux = nullptr, int64_t aux_ld = 0, const void* resid = nullptr,
+           int64_t resid_ld = 0) {
+  if (resid && (!host::aligned16(resid) || resid_ld % 8))
+    return fail(GKO_ERR_UNSUPPORTED, "the residual needs a 16-byte aligned base and a row stride that is a "
+                "multiple of 8");
   if (!host::aligned16(a) || !host::aligned16(b) || !host::aligned16(d) || (aux && !host::aligned16(aux)))
     return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs 16-byte aligned operand bases");
   if (aux && aux_ld % 8)
@@ -156,7 +160,7 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
 #ifndef GKO_GEMM_PAIR_MIN_M
 #define GKO_GEMM_PAIR_MIN_M 0x7fffffff
 #endif
-  const bool pair = M >= GKO_GEMM_PAIR_MIN_M && epi != kEpiAllReduce && !aux;
+  const bool pair = M >= GKO_GEMM_PAIR_MIN_M && epi != kEpiAllReduce && !aux && !resid;
   const int block_m = pair ? 2 * gemm::kBM : gemm::kBM;
   p.m_blocks = (int)((M + block_m - 1) / block_m);
   const int bn = gemm::block_n_out(epi);
@@ -199,6 +203,8 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
   p.red_ld = ldd;
   p.aux = aux;
   p.aux_ld = aux_ld;
+  p.resid = resid;
+  p.resid_ld = resid_ld;
   if (p.num_tiles == 0) return GKO_OK;
   if (pair) {
     if (dtype == GKO_BF16) return dispatch_pair<__nv_bfloat16>(epi, b_mn, ta, tb, td, p, stream);
@@ -369,4 +375,19 @@ extern "C" int gko_linear_swiglu_aux(int dtype, int64_t m, int64_t h, int64_t k,
     return run_tc(dtype, kEpiSwiglu, m, h, k, 2 * h, h, x, x_sm, w, w_sk, true, nullptr, kBiasNone, out, ldo, status,
                   s, nullptr, nullptr, 0, gate_up, ldg);
   return fail(GKO_ERR_UNSUPPORTED, "tensor-core SwiGLU needs a weight with unit stride in one dim");
+}
+
+extern "C" int gko_linear_residual(int dtype, int64_t m, int64_t n, int64_t k, const void* x, int64_t x_sm,
+                                   int64_t x_sk, const void* w, int64_t w_sn, int64_t w_sk, const void* resid,
+                                   int64_t resid_sm, void* out, int64_t ldo, unsigned int* status, void* stream) {
+  if (dtype != GKO_BF16 && dtype != GKO_F16)
+    return fail(GKO_ERR_UNSUPPORTED, "linear_residual runs on the bf16 / f16 tensor-core path only");
+  if (m < 0 || n < 0 || k < 0) return fail(GKO_ERR_INVALID, "negative GEMM size");
+  if (m == 0 || n == 0) return GKO_OK;
+  if (!out || !resid || (k && (!x || !w))) return fail(GKO_ERR_INVALID, "null operand pointer");
+  if (k == 0) return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs k > 0");
+  if (x_sk != 1 || w_sk != 1)
+    return fail(GKO_ERR_UNSUPPORTED, "linear_residual needs row-major x [m, k] and weight [n, k]");
+  return run_tc(dtype, kEpiNone, m, n, k, n, 0, x, x_sm, w, w_sn, false, nullptr, kBiasNone, out, ldo, status,
+                reinterpret_cast<cudaStream_t>(stream), nullptr, nullptr, 0, nullptr, 0, resid, resid_sm);
 }

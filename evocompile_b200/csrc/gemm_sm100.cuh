@@ -57,6 +57,10 @@ struct GemmParams {
   // up in [N_out, 2 N_out)); row stride aux_ld elements.
   void* aux;
   int64_t aux_ld;
+  // Optional residual R [M, N_out] (row stride resid_ld elements, NULL: none), added after the
+  // activation: D = act(A*B^T + bias) + R (kEpiNone / kEpiGelu / kEpiRelu). D may be R.
+  const void* resid;
+  int64_t resid_ld;
 };
 
 namespace gemm {
@@ -123,6 +127,25 @@ __device__ __forceinline__ void store_aux_row(void* aux, int64_t ld, int row, in
       reinterpret_cast<uint4*>(dst)[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
 }
 
+// Reads 32 values of row `row` from column `col` (16-byte loads; zeros past M / N).
+template <typename T>
+__device__ __forceinline__ void load_row32(const void* src, int64_t ld, int row, int col, int M, int N,
+                                           uint32_t (&v)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = 0u;
+  if (row >= M) return;
+  const T* s = static_cast<const T*>(src) + (int64_t)row * ld + col;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if (col + 8 * j < N) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(s) + j);
+      v[4 * j] = q.x;
+      v[4 * j + 1] = q.y;
+      v[4 * j + 2] = q.z;
+      v[4 * j + 3] = q.w;
+    }
+}
+
 template <typename T, int EPI, typename Release>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtensorMap* tm_d,
                                               uint32_t t_row, int row0, int col_base, int half,
@@ -167,6 +190,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
         tmem_ld32(t_row + col0, v);
         // one bias value per lane, broadcast across the row by shuffles
         const float bl = load_bias(p.bias, p.bias_kind, col_base + col0 + lane, p.N_out);
+        uint32_t rv[16];  // this lane's row of the residual (read while the TMEM load is in flight)
+        if (p.resid) load_row32<T>(p.resid, p.resid_ld, row0 + lane, col_base + col0, p.M, p.N_out, rv);
         tmem_wait_ld();
         uint32_t zp[16];
 #pragma unroll
@@ -180,6 +205,12 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
           } else if constexpr (EPI == kEpiRelu) {
             x0 = fmaxf(x0, 0.f);
             x1 = fmaxf(x1, 0.f);
+          }
+          if (p.resid) {
+            float r0, r1;
+            Cvt<T>::unpack(rv[i], r0, r1);
+            x0 += r0;
+            x1 += r1;
           }
           packed[i] = Cvt<T>::pack(x0, x1);
         }

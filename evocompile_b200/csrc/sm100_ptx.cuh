@@ -372,6 +372,10 @@ struct Cvt<__nv_bfloat16> {
     return *reinterpret_cast<uint32_t*>(&v);
   }
   static __device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ void unpack(uint32_t v, float& a, float& b) {
+    a = __uint_as_float(v << 16);
+    b = __uint_as_float(v & 0xFFFF0000u);
+  }
 };
 template <>
 struct Cvt<__half> {
@@ -380,6 +384,11 @@ struct Cvt<__half> {
     return *reinterpret_cast<uint32_t*>(&v);
   }
   static __device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ void unpack(uint32_t v, float& a, float& b) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&v));
+    a = f.x;
+    b = f.y;
+  }
 };
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,

@@ -515,3 +515,39 @@ def linear_allreduce(x, weight, out, multicast_ptr: int, peers_dev_ptr: int, wor
             )
         _lib.check(rc, "gko_linear_allreduce")
     return out
+
+
+def linear_residual(x, weight, resid, out=None):
+    """x @ weight^T + resid with the residual add in the GEMM epilogue (gko_linear_residual).
+
+    x [m, k] and weight [n, k] row-major, resid [m, n]; bf16 / f16. ``out`` (default: a new
+    tensor) may be ``resid`` itself for an in-place residual update. Returns out.
+    """
+    dev = _lib.require_cuda(x, weight, resid, out)
+    if x.dim() != 2 or weight.dim() != 2 or resid.dim() != 2:
+        raise RuntimeError("linear_residual: x [m, k], weight [n, k], resid [m, n]")
+    if x.dtype != weight.dtype or x.dtype != resid.dtype:
+        raise RuntimeError("linear_residual: x, weight, resid dtypes differ")
+    m, k = x.shape
+    n = weight.shape[0]
+    if weight.shape[1] != k or tuple(resid.shape) != (m, n):
+        raise RuntimeError(f"linear_residual: shape mismatch x {tuple(x.shape)} weight {tuple(weight.shape)} "
+                           f"resid {tuple(resid.shape)}")
+    if out is None:
+        out = torch.empty(m, n, device=x.device, dtype=x.dtype)
+    elif tuple(out.shape) != (m, n) or out.dtype != x.dtype or out.stride(1) != 1:
+        raise RuntimeError("linear_residual: out must be a row-major [m, n] tensor of x's dtype")
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    if weight.stride(1) != 1:
+        weight = weight.contiguous()
+    if resid.stride(1) != 1:
+        resid = resid.contiguous()
+    if m and n:
+        with torch.cuda.device(dev):
+            rc = _lib.load().gko_linear_residual(
+                _lib.dtype_code(x.dtype), m, n, k, _ptr(x), x.stride(0), 1, _ptr(weight), weight.stride(0), 1,
+                _ptr(resid), resid.stride(0), _ptr(out), out.stride(0), _status_ptr(dev), _stream(dev),
+            )
+        _lib.check(rc, "gko_linear_residual")
+    return out

@@ -243,6 +243,19 @@ int gko_linear_swiglu_aux(int dtype, int64_t m, int64_t h, int64_t k, const void
                           int64_t ldo, void* gate_up, int64_t ldg, unsigned int* status, void* stream);
 
 /*
+ * out[m, n] = x[m, k] @ w[n, k]^T + resid[m, n]: a linear layer with the residual add fused into
+ * its epilogue (one rounding to the output dtype). out may be resid (in place). Row-major x and w;
+ * row strides x_sm, resid_sm, ldo in elements (multiples of 8, 16-byte aligned bases); bf16 / f16.
+ * No reference counterpart. The reference's MLP rewrite ends in a plain projection
+ * (eval/rewrites/simple_gpt_silu_mul.py:18, c_proj) whose output the enclosing transformer block
+ * adds to its residual stream in a separate elementwise op; this entry does both in one kernel
+ * (used by the tensor-parallel block's down projection on one rank).
+ */
+int gko_linear_residual(int dtype, int64_t m, int64_t n, int64_t k, const void* x, int64_t x_sm, int64_t x_sk,
+                        const void* w, int64_t w_sn, int64_t w_sk, const void* resid, int64_t resid_sm, void* out,
+                        int64_t ldo, unsigned int* status, void* stream);
+
+/*
  * SwiGLU backward from the saved pre-activations: with s = sigmoid(g) and dy[rows, h],
  * d_gate_up[:, :h] = dy u s (1 + g (1 - s)) and d_gate_up[:, h:] = dy g s, where
  * gate_up = [g | u] is [rows, 2h]. Row strides in elements; bf16 / f16; h and strides

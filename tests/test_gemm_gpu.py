@@ -119,6 +119,25 @@ def test_gemm_swiglu_fp32():
     assert oracle.rel_err(out, ref) <= F32_TOL
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,n,k", [(300, 264, 256), (1, 8, 64), (129, 520, 128), (256, 512, 1024)])
+@pytest.mark.parametrize("in_place", [False, True])
+def test_linear_residual(dtype, m, n, k, in_place):
+    """x @ w^T + r with the residual add in the GEMM epilogue, also in place (out is r)."""
+    g = _gen(m + n + k + int(in_place))
+    x = _randn(g, m, k, dtype=dtype)
+    w = _randn(g, n, k, std=k ** -0.5, dtype=dtype)
+    r = _randn(g, m, n, dtype=dtype)
+    ref = x.float() @ w.float().t() + r.float()
+    rd = r.cuda()
+    out = ops.linear_residual(x.cuda(), w.cuda(), rd, out=rd if in_place else None)
+    assert out.shape == (m, n) and out.dtype == dtype
+    if in_place:
+        assert out.data_ptr() == rd.data_ptr()
+    _status_clean()
+    assert oracle.rel_err(out, ref) <= BF16_TOL
+
+
 def test_swiglu_mlp_small():
     g = _gen(9)
     x = _randn(g, 256, 512, dtype=torch.bfloat16)
