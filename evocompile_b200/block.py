@@ -11,8 +11,9 @@ row-parallel outputs are summed with an NCCL all-reduce. RMSNorm weights are rep
 
 Every GEMM is the tcgen05 kernel (the SwiGLU one fused), attention the tcgen05 FMHA reading
 q/k/v in place from the QKV output and writing [tokens, heads, d] for the o-projection,
-RMSNorm (+ residual add) and RoPE are the library's memory-bound kernels; on one rank the
-closing residual add runs in the down projection's epilogue (``ops.linear_residual``). With
+RMSNorm (+ residual add) and RoPE are the library's memory-bound kernels; the closing residual
+add runs in the down projection's epilogue (``ops.linear_residual``) on one rank, and with NCCL
+on rank 0 before the all-reduce. With
 ``comm="fused"`` the two row-parallel projections reduce their outputs across the group
 inside the GEMM over NVLink (``evocompile_b200.tp.FusedAllReduceLinear``); ``comm="nccl"``
 runs the GEMM and then an NCCL all-reduce. ``comm="auto"`` (the default) picks the fused
@@ -119,12 +120,19 @@ class TPBlock:
         self.comm = comm
         self._fused = {}
 
-    def _row_parallel(self, x, weight, slot):
-        """x @ weight^T summed over the group (row-parallel projection)."""
+    def _row_parallel(self, x, weight, slot, resid=None):
+        """x @ weight^T summed over the group (row-parallel projection), plus ``resid`` (replicated
+        on every rank, updated in place) when given."""
         if self.world == 1:
+            if resid is not None:
+                return ops.linear_residual(x, weight, resid, out=resid)
             return ops.linear(x, weight)
         if self.comm == "nccl":
-            y = ops.linear(x, weight)
+            # rank 0 adds the residual in its GEMM epilogue, so the all-reduce sums it in once
+            if resid is not None and torch.distributed.get_rank(self.group) == 0:
+                y = ops.linear_residual(x, weight, resid, out=resid)
+            else:
+                y = ops.linear(x, weight)
             torch.distributed.all_reduce(y, op=torch.distributed.ReduceOp.SUM, group=self.group)
             return y
         from .tp import FusedAllReduceLinear
@@ -134,7 +142,8 @@ class TPBlock:
         if f is None:  # collective: every rank builds it at the same call
             f = FusedAllReduceLinear(x.shape[0], weight.shape[0], x.dtype, x.device, self.group)
             self._fused[key] = f
-        return f(x, weight)
+        y = f(x, weight)
+        return y if resid is None else resid.add_(y)
 
     def forward(self, x: torch.Tensor, events=None) -> torch.Tensor:
         """x [B, S, d_model] (bf16) -> [B, S, d_model]. ``events`` (start, end) CUDA events, if
@@ -161,7 +170,5 @@ class TPBlock:
         g = ops.linear_swiglu(h2, w["w_gate_up"])                        # [T, ff_local]
         if events is not None:
             events[1].record()
-        if self.world == 1:  # down projection with the residual add in its epilogue, in place
-            return ops.linear_residual(g, w["w_down"], x1, out=x1).view(B, S, d)
-        dn = self._row_parallel(g, w["w_down"], 1)
-        return (x1 + dn).view(B, S, d)
+        # down projection + residual (in the GEMM epilogue on one rank, and on rank 0 with NCCL)
+        return self._row_parallel(g, w["w_down"], 1, resid=x1).view(B, S, d)
