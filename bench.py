@@ -545,7 +545,7 @@ class TPBlockWorkload(SwigluMLP):
         self.flop_step = self.cfg.flops(T, self.S)
         ff_l = self.cfg.d_ff // world
         self.flop_gateup = 2.0 * T * self.cfg.d_model * 2 * ff_l
-        self.launches_per_step = 8  # rmsnorm, qkv gemm, rope, fmha, o gemm, rmsnorm, gate/up, down
+        self.launches_per_step = 8  # rms stats, qkv gemm, rope, fmha, o gemm, rms stats, gate/up, down
         self.config = {
             "workload": "llama3-70b block prefill bf16: d_model 8192, 64 q / 8 kv heads, D 128, d_ff 28672, "
                         "B=4 S=4096; RMSNorm -> QKV -> RoPE(5e5) -> causal GQA FMHA -> o-proj -> residual -> "

@@ -88,6 +88,11 @@ SIGNATURES = {
         _int,
         [_int, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _vp],
     ),
+    "gko_rms_stats": (_int, [_int, _i64, _i64, _vp, _vp, _fl, _vp, _vp, _i64, _vp, _vp]),
+    "gko_linear_rowscale": (
+        _int,
+        [_int, _int, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp],
+    ),
     "gko_swiglu_bwd": (_int, [_int, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp]),
     "gko_silu_mul": (_int, [_int, _i64, _vp, _vp, _vp, _vp, _vp]),
     "gko_selftest_wait_timeout": (_int, [_vp, ctypes.c_longlong, _vp]),

@@ -11,7 +11,10 @@ row-parallel outputs are summed with an NCCL all-reduce. RMSNorm weights are rep
 
 Every GEMM is the tcgen05 kernel (the SwiGLU one fused), attention the tcgen05 FMHA reading
 q/k/v in place from the QKV output and writing [tokens, heads, d] for the o-projection,
-RMSNorm (+ residual add) and RoPE are the library's memory-bound kernels; the closing residual
+RoPE and the RMSNorm statistics (``ops.rms_stats``: 1/rms per token, plus the residual sum) are the
+library's memory-bound kernels; each RMSNorm is applied as a per-row scale in the epilogue of the
+GEMM that follows it, with its weight folded into that GEMM's weight (``ops.linear_rowscale``), so
+the normalised activations never go to HBM; the closing residual
 add runs in the down projection's epilogue (``ops.linear_residual``) on one rank, and with NCCL
 on rank 0 before the all-reduce. With
 ``comm="fused"`` the two row-parallel projections reduce their outputs across the group
@@ -111,7 +114,11 @@ class TPBlock:
     def __init__(self, local: dict, cfg: BlockConfig, group=None, comm: str = "auto"):
         if comm not in ("auto", "fused", "nccl"):
             raise ValueError(f"comm must be 'auto', 'fused' or 'nccl', got {comm!r}")
-        self.w = local
+        # RMSNorm runs as a per-row scale in the epilogue of the GEMM that follows it, with the
+        # norm weight folded into that GEMM's weight once here: w'[n, j] = w[n, j] * g[j]
+        self.w = dict(local)
+        self.w["wqkv_n"] = ops.fold_rmsnorm_weight(self.w.pop("wqkv"), local["attn_norm"])
+        self.w["w_gate_up_n"] = ops.fold_rmsnorm_weight(self.w.pop("w_gate_up"), local["mlp_norm"])
         self.cfg = cfg
         self.group = group
         self.world = 1 if group is None else torch.distributed.get_world_size(group)
@@ -153,8 +160,8 @@ class TPBlock:
         T, hd = B * S, cfg.head_dim
         hq, hkv = w["hq_local"], w["hkv_local"]
         x2 = x.reshape(T, d)
-        h = ops.rmsnorm(x2, w["attn_norm"], cfg.eps)
-        qkv = ops.linear(h, w["wqkv"])                                    # [T, (hq + 2 hkv) * D]
+        inv1 = ops.rms_stats(x2, cfg.eps)                                 # 1/rms per token (fp32)
+        qkv = ops.linear_rowscale(x2, w["wqkv_n"], inv1)                  # rmsnorm(x) Wqkv^T  [T, (hq + 2 hkv) * D]
         q = qkv[:, : hq * hd].view(T, hq, hd)
         k = qkv[:, hq * hd: (hq + hkv) * hd].view(T, hkv, hd)
         v = qkv[:, (hq + hkv) * hd:].view(T, hkv, hd)
@@ -164,10 +171,10 @@ class TPBlock:
         attn = torch.empty(T, hq, hd, device=x.device, dtype=x.dtype)
         ops.fmha_fwd(as4(q), as4(k), as4(v), None, hd ** -0.5, 1, out=as4(attn))
         o = self._row_parallel(attn.view(T, hq * hd), w["wo"], 0)          # row-parallel partial -> sum
-        h2, x1 = ops.rmsnorm(o, w["mlp_norm"], cfg.eps, residual=x2, return_sum=True)
+        inv2, x1 = ops.rms_stats(o, cfg.eps, residual=x2)               # x1 = x + o, 1/rms(x1)
         if events is not None:
             events[0].record()
-        g = ops.linear_swiglu(h2, w["w_gate_up"])                        # [T, ff_local]
+        g = ops.linear_rowscale(x1, w["w_gate_up_n"], inv2, swiglu=True)  # SwiGLU(rmsnorm(x1) W^T) [T, ff_local]
         if events is not None:
             events[1].record()
         # down projection + residual (in the GEMM epilogue on one rank, and on rank 0 with NCCL)

@@ -104,7 +104,7 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
            const void* bias, int bias_kind, void* d, int64_t ldd, unsigned* status,
            cudaStream_t stream, void* red_mc = nullptr, void* const* red_peers = nullptr,
            int red_world = 0, void* aux = nullptr, int64_t aux_ld = 0, const void* resid = nullptr,
-           int64_t resid_ld = 0) {
+           int64_t resid_ld = 0, const float* row_scale = nullptr) {
   if (resid && (!host::aligned16(resid) || resid_ld % 8))
     return fail(GKO_ERR_UNSUPPORTED, "the residual needs a 16-byte aligned base and a row stride that is a "
                 "multiple of 8");
@@ -160,7 +160,7 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
 #ifndef GKO_GEMM_PAIR_MIN_M
 #define GKO_GEMM_PAIR_MIN_M 0x7fffffff
 #endif
-  const bool pair = M >= GKO_GEMM_PAIR_MIN_M && epi != kEpiAllReduce && !aux && !resid;
+  const bool pair = M >= GKO_GEMM_PAIR_MIN_M && epi != kEpiAllReduce && !aux && !resid && !row_scale;
   const int block_m = pair ? 2 * gemm::kBM : gemm::kBM;
   p.m_blocks = (int)((M + block_m - 1) / block_m);
   const int bn = gemm::block_n_out(epi);
@@ -205,6 +205,7 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
   p.aux_ld = aux_ld;
   p.resid = resid;
   p.resid_ld = resid_ld;
+  p.row_scale = row_scale;
   if (p.num_tiles == 0) return GKO_OK;
   if (pair) {
     if (dtype == GKO_BF16) return dispatch_pair<__nv_bfloat16>(epi, b_mn, ta, tb, td, p, stream);
@@ -390,4 +391,26 @@ extern "C" int gko_linear_residual(int dtype, int64_t m, int64_t n, int64_t k, c
     return fail(GKO_ERR_UNSUPPORTED, "linear_residual needs row-major x [m, k] and weight [n, k]");
   return run_tc(dtype, kEpiNone, m, n, k, n, 0, x, x_sm, w, w_sn, false, nullptr, kBiasNone, out, ldo, status,
                 reinterpret_cast<cudaStream_t>(stream), nullptr, nullptr, 0, nullptr, 0, resid, resid_sm);
+}
+
+extern "C" int gko_linear_rowscale(int dtype, int swiglu, int64_t m, int64_t n, int64_t k, const void* x,
+                                   int64_t x_sm, int64_t x_sk, const void* w, int64_t w_sn, int64_t w_sk,
+                                   const float* row_scale, void* out, int64_t ldo, unsigned int* status,
+                                   void* stream) {
+  if (dtype != GKO_BF16 && dtype != GKO_F16)
+    return fail(GKO_ERR_UNSUPPORTED, "linear_rowscale runs on the bf16 / f16 tensor-core path only");
+  if (m < 0 || n < 0 || k < 0) return fail(GKO_ERR_INVALID, "negative GEMM size");
+  if (m == 0 || n == 0) return GKO_OK;
+  if (!out || !row_scale || (k && (!x || !w))) return fail(GKO_ERR_INVALID, "null operand pointer");
+  if (k == 0) return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs k > 0");
+  if (x_sk != 1 || w_sk != 1)
+    return fail(GKO_ERR_UNSUPPORTED, "linear_rowscale needs row-major x [m, k] and weight [rows, k]");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (swiglu) {
+    if (n % 8) return fail(GKO_ERR_UNSUPPORTED, "SwiGLU needs h %% 8 == 0");
+    return run_tc(dtype, kEpiSwiglu, m, n, k, 2 * n, n, x, x_sm, w, w_sn, false, nullptr, kBiasNone, out, ldo,
+                  status, s, nullptr, nullptr, 0, nullptr, 0, nullptr, 0, row_scale);
+  }
+  return run_tc(dtype, kEpiNone, m, n, k, n, 0, x, x_sm, w, w_sn, false, nullptr, kBiasNone, out, ldo, status, s,
+                nullptr, nullptr, 0, nullptr, 0, nullptr, 0, row_scale);
 }

@@ -61,6 +61,10 @@ struct GemmParams {
   // activation: D = act(A*B^T + bias) + R (kEpiNone / kEpiGelu / kEpiRelu). D may be R.
   const void* resid;
   int64_t resid_ld;
+  // Optional per-row scale s [M] (fp32, NULL: none) applied to the accumulator first:
+  // D = act(s_r * (A*B^T) + bias) + R; SwiGLU: silu(s_r g) * (s_r u). With s = 1/rms(A row)
+  // and the RMSNorm weight folded into B, the GEMM computes rmsnorm(A) * B^T.
+  const float* row_scale;
 };
 
 namespace gemm {
@@ -163,11 +167,19 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
     for (int h = 0; h < 2; ++h) {
       const int col0 = c * 64 + h * 32;
       uint32_t packed[16];
+      const float rs = (p.row_scale && row0 + lane < p.M) ? __ldg(p.row_scale + row0 + lane) : 1.f;
       if constexpr (EPI == kEpiSwiglu) {
         uint32_t g[32], u[32];
         tmem_ld32(t_row + col0, g);
         tmem_ld32(t_row + 128 + col0, u);
         tmem_wait_ld();
+        if (p.row_scale) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            g[i] = __float_as_uint(__uint_as_float(g[i]) * rs);
+            u[i] = __float_as_uint(__uint_as_float(u[i]) * rs);
+          }
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
@@ -196,8 +208,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
         uint32_t zp[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float x0 = __uint_as_float(v[2 * i]) + __shfl_sync(0xffffffffu, bl, 2 * i);
-          float x1 = __uint_as_float(v[2 * i + 1]) + __shfl_sync(0xffffffffu, bl, 2 * i + 1);
+          float x0 = fmaf(__uint_as_float(v[2 * i]), rs, __shfl_sync(0xffffffffu, bl, 2 * i));
+          float x1 = fmaf(__uint_as_float(v[2 * i + 1]), rs, __shfl_sync(0xffffffffu, bl, 2 * i + 1));
           zp[i] = Cvt<T>::pack(x0, x1);
           if constexpr (EPI == kEpiGelu) {
             x0 = gelu_erf(x0);

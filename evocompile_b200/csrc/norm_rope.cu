@@ -1,5 +1,7 @@
 // Memory-bound pieces of the transformer block around the fused operators:
 //   gko_rmsnorm  y = rmsnorm(x (+ r)) * w, optionally writing the residual sum x + r
+//   gko_rms_stats  inv[row] = 1 / sqrt(mean((x + r)^2) + eps) only (optionally writing x + r): the
+//                statistics a GEMM needs to apply RMSNorm as a per-row scale in its epilogue
 //   gko_rope     rotary position embedding applied in place to q / k heads
 // Both are HBM-bound: 16-byte vector loads/stores, fp32 arithmetic.
 #include <cuda_bf16.h>
@@ -62,7 +64,7 @@ template <typename T, int VPT>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ r,
                                                                const T* __restrict__ w, T* __restrict__ y,
                                                                T* __restrict__ sum_out, int cols, int64_t ld,
-                                                               float eps) {
+                                                               float eps, float* __restrict__ inv_out) {
   const int64_t row = blockIdx.x;
   const int nvec = cols / 8;
   float v[VPT][8];
@@ -102,6 +104,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const T* __restri
 #pragma unroll
   for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
   const float inv = rsqrtf(tot / (float)cols + eps);
+  if (inv_out && threadIdx.x == 0) inv_out[row] = inv;
+  if (!y) return;  // statistics only
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int vi = threadIdx.x + i * kNormThreads;
@@ -164,17 +168,17 @@ using gko::host::fail;
 namespace {
 template <typename T>
 void launch_rmsnorm(int vpt, int64_t rows, const void* x, const void* r, const void* w, void* y, void* sum_out,
-                    int cols, int64_t ld, float eps, cudaStream_t s) {
+                    int cols, int64_t ld, float eps, cudaStream_t s, float* inv_out = nullptr) {
   const T* xp = static_cast<const T*>(x);
   const T* rp = static_cast<const T*>(r);
   const T* wp = static_cast<const T*>(w);
   T* yp = static_cast<T*>(y);
   T* sp = static_cast<T*>(sum_out);
   const unsigned g = (unsigned)rows;
-  if (vpt == 1) rmsnorm_kernel<T, 1><<<g, kNormThreads, 0, s>>>(xp, rp, wp, yp, sp, cols, ld, eps);
-  else if (vpt == 2) rmsnorm_kernel<T, 2><<<g, kNormThreads, 0, s>>>(xp, rp, wp, yp, sp, cols, ld, eps);
-  else if (vpt == 4) rmsnorm_kernel<T, 4><<<g, kNormThreads, 0, s>>>(xp, rp, wp, yp, sp, cols, ld, eps);
-  else rmsnorm_kernel<T, 8><<<g, kNormThreads, 0, s>>>(xp, rp, wp, yp, sp, cols, ld, eps);
+  if (vpt == 1) rmsnorm_kernel<T, 1><<<g, kNormThreads, 0, s>>>(xp, rp, wp, yp, sp, cols, ld, eps, inv_out);
+  else if (vpt == 2) rmsnorm_kernel<T, 2><<<g, kNormThreads, 0, s>>>(xp, rp, wp, yp, sp, cols, ld, eps, inv_out);
+  else if (vpt == 4) rmsnorm_kernel<T, 4><<<g, kNormThreads, 0, s>>>(xp, rp, wp, yp, sp, cols, ld, eps, inv_out);
+  else rmsnorm_kernel<T, 8><<<g, kNormThreads, 0, s>>>(xp, rp, wp, yp, sp, cols, ld, eps, inv_out);
 }
 }  // namespace
 
@@ -230,4 +234,28 @@ extern "C" int gko_rope(int dtype, int64_t tokens, int64_t heads, int64_t head_d
     rope_kernel<__half><<<(unsigned)blocks, 256, 0, s>>>(static_cast<__half*>(x), tokens, (int)heads, (int)head_dim,
                                                          st_token, st_head, positions, (int)seq_len, l2t);
   return gko::host::cuda_check(cudaGetLastError(), "rope launch");
+}
+
+extern "C" int gko_rms_stats(int dtype, int64_t rows, int64_t cols, const void* x, const void* residual, float eps,
+                             void* sum_out, float* inv_out, int64_t ld, unsigned int* status, void* stream) {
+  (void)status;
+  if (dtype != GKO_BF16 && dtype != GKO_F16) return fail(GKO_ERR_UNSUPPORTED, "rms_stats takes bf16 or f16");
+  if (rows < 0 || cols <= 0) return fail(GKO_ERR_INVALID, "bad rms_stats sizes");
+  if (rows == 0) return GKO_OK;
+  if (cols % 8 || ld % 8 || ld < cols)
+    return fail(GKO_ERR_UNSUPPORTED, "rms_stats needs cols and row stride multiples of 8 (ld >= cols)");
+  if (cols > kNormThreads * kMaxVecPerThread * 8) return fail(GKO_ERR_UNSUPPORTED, "rms_stats supports cols <= 16384");
+  if (!x || !inv_out) return fail(GKO_ERR_INVALID, "null pointer argument");
+  if (!gko::host::aligned16(x) || (residual && !gko::host::aligned16(residual)) ||
+      (sum_out && !gko::host::aligned16(sum_out)))
+    return fail(GKO_ERR_UNSUPPORTED, "rms_stats needs 16-byte aligned buffers");
+  if (rows > 0x7fffffffll) return fail(GKO_ERR_UNSUPPORTED, "too many rows");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t per = (cols / 8 + kNormThreads - 1) / kNormThreads;
+  const int vpt = per <= 1 ? 1 : per <= 2 ? 2 : per <= 4 ? 4 : 8;
+  if (dtype == GKO_BF16)
+    launch_rmsnorm<__nv_bfloat16>(vpt, rows, x, residual, nullptr, nullptr, sum_out, (int)cols, ld, eps, s, inv_out);
+  else
+    launch_rmsnorm<__half>(vpt, rows, x, residual, nullptr, nullptr, sum_out, (int)cols, ld, eps, s, inv_out);
+  return gko::host::cuda_check(cudaGetLastError(), "rms_stats launch");
 }

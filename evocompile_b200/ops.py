@@ -551,3 +551,62 @@ def linear_residual(x, weight, resid, out=None):
             )
         _lib.check(rc, "gko_linear_residual")
     return out
+
+
+def rms_stats(x, eps=1e-5, residual=None):
+    """Per-row 1 / sqrt(mean(v^2) + eps) of v = x (+ residual), fp32 [rows]; with a residual also
+    returns v (the updated residual stream) as (inv, v). x [..., cols] bf16 / f16."""
+    dev = _lib.require_cuda(x, residual)
+    cols = x.shape[-1]
+    x2 = x.reshape(-1, cols).contiguous()
+    r2 = residual.reshape(-1, cols).contiguous() if residual is not None else None
+    inv = torch.empty(x2.shape[0], device=dev, dtype=torch.float32)
+    total = torch.empty(x2.shape, device=dev, dtype=x.dtype) if r2 is not None else None
+    if x2.shape[0]:
+        with torch.cuda.device(dev):
+            rc = _lib.load().gko_rms_stats(
+                _lib.dtype_code(x.dtype), x2.shape[0], cols, _ptr(x2), _ptr(r2), float(eps), _ptr(total), _ptr(inv),
+                cols, _status_ptr(dev), _stream(dev),
+            )
+        _lib.check(rc, "gko_rms_stats")
+    if r2 is not None:
+        return inv, total.reshape(x.shape)
+    return inv
+
+
+def fold_rmsnorm_weight(weight, norm_weight):
+    """w'[n, j] = w[n, j] * g[j] (computed in fp32, rounded once): the projection weight that,
+    with rms_stats' per-row scale in linear_rowscale, applies RMSNorm(g) before the projection."""
+    return (weight.float() * norm_weight.float().view(1, -1)).to(weight.dtype)
+
+
+def linear_rowscale(x, weight, row_scale, swiglu: bool = False):
+    """out = row_scale[:, None] * (x @ weight^T) on the tensor-core GEMM (the scale applied to the
+    accumulator in the epilogue); with swiglu, weight = [Wg; Wu] (2H, K) and
+    out = silu(s x Wg^T) * (s x Wu^T) (rows, H). x [rows, K] row-major, row_scale fp32 [rows]."""
+    dev = _lib.require_cuda(x, weight, row_scale)
+    if x.dim() != 2 or weight.dim() != 2 or row_scale.dim() != 1:
+        raise RuntimeError("linear_rowscale: x [m, k], weight [n, k], row_scale [m]")
+    if x.dtype != weight.dtype or row_scale.dtype != torch.float32:
+        raise RuntimeError("linear_rowscale: x and weight share a dtype; row_scale is float32")
+    m, k = x.shape
+    if weight.shape[1] != k or row_scale.shape[0] != m:
+        raise RuntimeError(f"linear_rowscale: shape mismatch x {tuple(x.shape)} weight {tuple(weight.shape)} "
+                           f"row_scale {tuple(row_scale.shape)}")
+    if swiglu and weight.shape[0] % 2:
+        raise RuntimeError("linear_rowscale: the SwiGLU weight has an even number of rows [Wg; Wu]")
+    n = weight.shape[0] // 2 if swiglu else weight.shape[0]
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    if weight.stride(1) != 1:
+        weight = weight.contiguous()
+    row_scale = row_scale.contiguous()
+    out = torch.empty(m, n, device=x.device, dtype=x.dtype)
+    if m and n:
+        with torch.cuda.device(dev):
+            rc = _lib.load().gko_linear_rowscale(
+                _lib.dtype_code(x.dtype), int(bool(swiglu)), m, n, k, _ptr(x), x.stride(0), 1, _ptr(weight),
+                weight.stride(0), 1, _ptr(row_scale), _ptr(out), out.stride(0), _status_ptr(dev), _stream(dev),
+            )
+        _lib.check(rc, "gko_linear_rowscale")
+    return out

@@ -294,6 +294,23 @@ int gko_silu_mul(int dtype, int64_t n, const void* x, const void* y, void* out,
                  unsigned int* status, void* stream);
 
 /*
+ * RMSNorm folded into the following GEMM. gko_rms_stats writes inv[row] = 1 / sqrt(mean(v^2) + eps)
+ * of v = x + residual (residual may be NULL; sum_out, when not NULL, receives v) and nothing
+ * else; gko_linear_rowscale then computes out = (inv[row] * (x @ w^T)) with the RMSNorm weight
+ * folded into w beforehand (w'[n, j] = w[n, j] * g[j]), which equals rmsnorm(x) * g @ w^T. With
+ * swiglu != 0, w is [2n, k] = [Wg; Wu] and out[m, n] = silu(inv x Wg^T) * (inv x Wu^T). Row-major
+ * x and w, bf16 / f16, strides in elements (multiples of 8), inv fp32 on the device.
+ *
+ * No reference counterpart: the block's RMSNorm prologue (the reference has no transformer block
+ * on its kernel path); this skips writing the normalised activations to HBM.
+ */
+int gko_rms_stats(int dtype, int64_t rows, int64_t cols, const void* x, const void* residual, float eps,
+                  void* sum_out, float* inv_out, int64_t ld, unsigned int* status, void* stream);
+int gko_linear_rowscale(int dtype, int swiglu, int64_t m, int64_t n, int64_t k, const void* x, int64_t x_sm,
+                        int64_t x_sk, const void* w, int64_t w_sn, int64_t w_sk, const float* row_scale, void* out,
+                        int64_t ldo, unsigned int* status, void* stream);
+
+/*
  * y = rmsnorm(x + residual) * weight over rows of `cols` elements (row stride ld),
  * rmsnorm(v) = v / sqrt(mean(v^2) + eps). residual may be NULL; when sum_out is
  * not NULL it receives x + residual (the updated residual stream). bf16/f16,

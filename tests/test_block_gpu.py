@@ -29,6 +29,44 @@ def test_rmsnorm(rows, cols, with_res):
     assert oracle.rel_err(tot, xs) <= 1e-2
 
 
+@pytest.mark.parametrize("rows,cols", [(1, 8), (300, 8192), (5, 16384)])
+@pytest.mark.parametrize("with_res", [False, True])
+def test_rms_stats(rows, cols, with_res):
+    g = torch.Generator().manual_seed(3 * rows + cols)
+    x = torch.randn(rows, cols, generator=g).to(torch.bfloat16)
+    r = torch.randn(rows, cols, generator=g).to(torch.bfloat16) if with_res else None
+    dev = torch.device("cuda", 0)
+    res = ops.rms_stats(x.to(dev), 1e-5, residual=None if r is None else r.to(dev))
+    inv, tot = res if with_res else (res, None)
+    xs = x.float() + (r.float() if r is not None else 0)
+    ref = torch.rsqrt(xs.pow(2).mean(-1) + 1e-5)
+    assert inv.dtype == torch.float32 and inv.shape == (rows,)
+    assert ((inv.cpu() - ref).abs() / ref).max().item() <= 1e-4
+    if with_res:
+        assert oracle.rel_err(tot, xs) <= 1e-2
+
+
+@pytest.mark.parametrize("swiglu", [False, True])
+@pytest.mark.parametrize("m,k,n", [(300, 512, 264), (1, 256, 64), (129, 1024, 520)])
+def test_rmsnorm_folded_linear(swiglu, m, k, n):
+    """rmsnorm(x) * g @ W^T as rms_stats + a GEMM whose epilogue scales each row, with g folded
+    into W (non-unit g, so the fold is exercised)."""
+    gen = torch.Generator().manual_seed(m + k + n + int(swiglu))
+    x = torch.randn(m, k, generator=gen).to(torch.bfloat16)
+    gnorm = (1 + 0.2 * torch.randn(k, generator=gen)).to(torch.bfloat16)
+    w = (torch.randn(2 * n if swiglu else n, k, generator=gen) * k ** -0.5).to(torch.bfloat16)
+    dev = torch.device("cuda", 0)
+    xd = x.to(dev)
+    out = ops.linear_rowscale(xd, ops.fold_rmsnorm_weight(w.to(dev), gnorm.to(dev)), ops.rms_stats(xd, 1e-5),
+                              swiglu=swiglu)
+    h = oracle.rmsnorm(x, gnorm, 1e-5)
+    z = h @ w.float().t()
+    ref = torch.nn.functional.silu(z[:, :n]) * z[:, n:] if swiglu else z
+    assert out.shape == (m, n)
+    assert _lib.read_status(dev) == 0
+    assert oracle.rel_err(out, ref) <= TOL
+
+
 @pytest.mark.parametrize("heads,d", [(4, 64), (8, 128)])
 def test_rope_strided_in_place(heads, d):
     g = torch.Generator().manual_seed(heads)
