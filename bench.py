@@ -13,6 +13,9 @@ Other workloads (for measurement; the default line uses swiglu):
   addmm_gelu   X[8192, 4096] @ W[14336, 4096]^T + b, exact GELU
   fmha_causal  causal attention B=8 H=32 S=4096 D=128 in [B, S, H, D] (heads sharded at N > 1)
   fmha_varlen  GQA varlen causal, Hq=64 Hkv=8 D=128, 16 sequences L ~ U[512, 8192] (seed 0)
+  fmha_bwd     attention backward of the fmha_causal configuration
+  swiglu_train forward + backward of the fused gate/up SwiGLU (training form) at the Llama-3-8B shape
+  tp_block     Llama-3-70B block prefill B=4 S=4096, tensor parallel over the ranks
 
 Timing: W untimed warm-up steps, then K steps between a barrier +
 synchronize on both sides, timed with CUDA events on the launching stream;
@@ -183,7 +186,7 @@ class SwigluMLP:
         self.config = {
             "workload": "swiglu_mlp llama3-8b shape: X[8192,4096] bf16, W_gate/W_up[14336,4096] packed [28672,4096], "
                         "W_down[4096,14336]; step = fused gate/up+SwiGLU kernel + down-proj GEMM",
-            "model": "Llama-3-8B MLP (synthetic random-init weights N(0,0.02), X ~ N(0,1))",
+            "inputs": "synthetic: weights N(0,0.02) at Llama-3-8B MLP shapes, X ~ N(0,1)",
             "tokens_per_gpu": self.T, "global_batch": self.T * world, "seq_len": None,
             "parallelism": f"dp{world} (token-sharded, weights replicated)",
             "l2": "operands 0.64 GB per GPU > 126 MB L2; no flush",
@@ -552,7 +555,7 @@ class TPBlockWorkload(SwigluMLP):
             "workload": "llama3-70b block prefill bf16: d_model 8192, 64 q / 8 kv heads, D 128, d_ff 28672, "
                         "B=4 S=4096; RMSNorm -> QKV -> RoPE(5e5) -> causal GQA FMHA -> o-proj -> residual -> "
                         "RMSNorm -> SwiGLU -> down -> residual",
-            "model": "Llama-3-70B block (synthetic random-init weights N(0,0.02), x ~ N(0,1))",
+            "inputs": "synthetic: weights N(0,0.02) at Llama-3-70B block shapes, x ~ N(0,1)",
             "global_batch": self.B, "seq_len": self.S, "tokens": T,
             "parallelism": f"tp{world} (column-parallel QKV / gate-up, row-parallel o / down; row-parallel sums: "
                            + ("none" if world == 1 else "inside the GEMM over NVLink (multicast reduction)"
