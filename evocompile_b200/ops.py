@@ -192,9 +192,23 @@ def silu_mul(x, y):
     return out
 
 
+def _check_norm_args(name, x, residual=None, weight=None):
+    """The norm kernels read rows x cols elements of x, of the residual and cols of the weight, all in x's
+    dtype: a residual or weight of another shape or dtype would be read out of bounds or misread."""
+    if x.dim() < 1 or x.shape[-1] == 0:
+        raise RuntimeError(f"{name}: x needs a non-empty last dim, got {tuple(x.shape)}")
+    if residual is not None and (residual.shape != x.shape or residual.dtype != x.dtype):
+        raise RuntimeError(f"{name}: residual {tuple(residual.shape)} {residual.dtype} must match x "
+                           f"{tuple(x.shape)} {x.dtype}")
+    if weight is not None and (weight.numel() != x.shape[-1] or weight.dtype != x.dtype):
+        raise RuntimeError(f"{name}: weight {tuple(weight.shape)} {weight.dtype} must have {x.shape[-1]} "
+                           f"elements of x's dtype {x.dtype}")
+
+
 def rmsnorm(x, weight, eps=1e-5, residual=None, return_sum=False):
     """rmsnorm(x (+ residual)) * weight over the last dim; with return_sum also x + residual."""
     dev = _lib.require_cuda(x, weight, residual)
+    _check_norm_args("rmsnorm", x, residual, weight)
     cols = x.shape[-1]
     x2 = x.reshape(-1, cols).contiguous()
     r2 = residual.reshape(-1, cols).contiguous() if residual is not None else None
@@ -219,10 +233,12 @@ def rope_(x, theta=500000.0, positions=None, seq_len=None):
 
     Position of token t: positions[t] (int32 tensor) or t % seq_len.
     """
-    dev = _lib.require_cuda(x, positions)
     if x.dim() != 3 or x.stride(-1) != 1:
         raise RuntimeError("rope_: x must be [tokens, heads, head_dim] with unit stride along head_dim")
     t, h, d = x.shape
+    if positions is not None and positions.numel() != t:
+        raise RuntimeError(f"rope_: positions holds {positions.numel()} entries for {t} tokens")
+    dev = _lib.require_cuda(x, positions)
     pos = positions.to(torch.int32).contiguous() if positions is not None else None
     if pos is None and not seq_len:
         seq_len = t
@@ -557,6 +573,7 @@ def rms_stats(x, eps=1e-5, residual=None):
     """Per-row 1 / sqrt(mean(v^2) + eps) of v = x (+ residual), fp32 [rows]; with a residual also
     returns v (the updated residual stream) as (inv, v). x [..., cols] bf16 / f16."""
     dev = _lib.require_cuda(x, residual)
+    _check_norm_args("rms_stats", x, residual)
     cols = x.shape[-1]
     x2 = x.reshape(-1, cols).contiguous()
     r2 = residual.reshape(-1, cols).contiguous() if residual is not None else None

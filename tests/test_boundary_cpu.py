@@ -86,6 +86,27 @@ def test_ops_refuse_cpu_tensors():
         torch.ops.gko.fused_sdpa_pair(q, q, q, torch.empty(0), 0.1, 0, 0, 0.0)
 
 
+def test_norm_ops_refuse_mismatched_residual_and_weight():
+    """The RMSNorm kernels read a residual of x's shape and a weight of x's last dim in x's dtype;
+    anything else is refused on the host before a launch could read out of bounds."""
+    from evocompile_b200 import ops
+
+    x = torch.zeros(6, 64, dtype=torch.bfloat16)
+    ops._check_norm_args("rms_stats", x, torch.zeros_like(x))
+    ops._check_norm_args("rmsnorm", x, None, torch.ones(64, dtype=torch.bfloat16))
+    with pytest.raises(RuntimeError, match="residual"):
+        ops._check_norm_args("rms_stats", x, torch.zeros(5, 64, dtype=torch.bfloat16))
+    with pytest.raises(RuntimeError, match="residual"):
+        ops._check_norm_args("rms_stats", x, torch.zeros(6, 64, dtype=torch.float16))
+    with pytest.raises(RuntimeError, match="weight"):
+        ops._check_norm_args("rmsnorm", x, None, torch.ones(32, dtype=torch.bfloat16))
+    with pytest.raises(RuntimeError, match="weight"):
+        ops._check_norm_args("rmsnorm", x, None, torch.ones(64, dtype=torch.float32))
+    # rope_ checks the positions length before it reaches the device check
+    with pytest.raises(RuntimeError, match="positions"):
+        ops.rope_(torch.zeros(4, 2, 64).as_strided((4, 2, 64), (128, 64, 1)), positions=torch.zeros(3))
+
+
 def _count(gm, op):
     return sum(1 for n in gm.graph.nodes if n.target == op)
 
