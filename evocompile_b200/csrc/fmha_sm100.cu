@@ -492,7 +492,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = wait_bounded(bar_ofinal + 8 * t, 0, abort_flag, p.status, kStatusTimeoutSoftmax);
       tc_fence_after();
     }
-    const bool write = qi < len_q;
+    // varlen: rows outside [0, total_q) (cu_seqlens past the packed tokens) are never written
+    const bool write = qi < len_q && (!VARLEN || (row_q0 >= 0 && row_q0 + qi < p.total_q));
     T* orow;
     if constexpr (VARLEN)
       orow = reinterpret_cast<T*>(p.out) + ((int64_t)(row_q0 + qi) * p.hq + h) * D;

@@ -355,7 +355,9 @@ def fmha_varlen_fwd(q, k, v, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqle
                     causal=0, window=0, softcap=0.0):
     """Attention over packed sequences -> (out [tq, hq, d], lse f32 [hq, tq]).
 
-    q [tq, hq, d], k/v [tk, hkv, d]; cu_seqlens_* int32 [b + 1] on the device.
+    q [tq, hq, d], k/v [tk, hkv, d]; cu_seqlens_* int32 [b + 1] on the device, non-decreasing from 0 to the
+    token count (not checked on the host, which would need a device sync; the kernel writes no row outside
+    [0, tq)), and max_seqlen_q at least the longest query sequence.
     """
     dev = _lib.require_cuda(q, k, v, cu_seqlens_q, cu_seqlens_k)
     if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
@@ -454,7 +456,8 @@ def fmha_bwd(q, k, v, attn_bias, out, lse, dout, scale=None, causal=0, window=0,
 
 def fmha_varlen_bwd(q, k, v, out, lse, dout, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, scale=None,
                     causal=0, window=0, softcap=0.0):
-    """Backward of ``fmha_varlen_fwd`` -> (dq [tq, hq, d], dk, dv [tk, hkv, d])."""
+    """Backward of ``fmha_varlen_fwd`` -> (dq [tq, hq, d], dk, dv [tk, hkv, d]). The kernels trust
+    cu_seqlens: they must be non-decreasing from 0 to the token counts, as for the forward."""
     dev = _lib.require_cuda(q, k, v, out, lse, dout, cu_seqlens_q, cu_seqlens_k)
     if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
         raise RuntimeError("fmha_varlen_bwd: q, k, v must be 3-D [tokens, heads, d]")
