@@ -86,6 +86,7 @@ struct Params {
   int64_t dv_sz, dv_sh, dv_ss;
   const int* cu_q;
   const int* cu_k;
+  int total_q, total_k;  // varlen: packed query / key tokens (every row index stays below them)
   unsigned* status;
 };
 
@@ -106,12 +107,24 @@ struct RowParams {
   int64_t dq_sz, dq_sh, dq_ss;
   float scale;
   const int* cu_q;
+  int total_q;  // varlen: packed query tokens
 };
 
-// First 64-query block of sequence b in a head's run of blocks (varlen): blocks of
-// consecutive sequences never overlap because ceil(a/64) + ceil(l/64) <= ceil((a+l)/64) + 1.
-__device__ __forceinline__ int64_t varlen_block_base(const int* cu_q, int b) {
-  return (int64_t)((cu_q[b] + kBM - 1) / kBM) + b;
+// Rows [row0, row0 + len) of sequence b (varlen), clamped to the packed tokens [0, total):
+// whatever cu_seqlens hold, no row index formed from them leaves the tensors.
+__device__ __forceinline__ void varlen_rows(const int* cu, int b, int total, int& row0, int& len) {
+  const int a = min(max(cu[b], 0), total);
+  const int e = min(max(cu[b + 1], a), total);
+  row0 = a;
+  len = e - a;
+}
+
+// First 64-query block of sequence b in a head's run of blocks (varlen), from its clamped first
+// row a: blocks of consecutive sequences never overlap because ceil(a/64) + ceil(l/64) <=
+// ceil((a+l)/64) + 1, and with a + l <= total every block index stays below
+// ceil(total/64) + batch, inside the workspace's ceil(total/64) + batch + 1 blocks per head.
+__device__ __forceinline__ int64_t varlen_block_base(int row_q0, int b) {
+  return (int64_t)((row_q0 + kBM - 1) / kBM) + b;
 }
 
 __device__ __forceinline__ float bias_at(const Params& p, int z, int h, int q, int k) {
@@ -161,10 +174,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n0 = (int)blockIdx.x * kBN;  // first key of this CTA (sequence-local)
   int len_q, len_k, row_q0, row_k0;
   if constexpr (VARLEN) {
-    row_q0 = p.cu_q[zb];
-    len_q = p.cu_q[zb + 1] - row_q0;
-    row_k0 = p.cu_k[zb];
-    len_k = p.cu_k[zb + 1] - row_k0;
+    varlen_rows(p.cu_q, zb, p.total_q, row_q0, len_q);
+    varlen_rows(p.cu_k, zb, p.total_k, row_k0, len_k);
   } else {
     row_q0 = 0;
     len_q = p.sq;
@@ -183,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int jb_lo = q_lo / kBM;
   const int nq = q_hi > q_lo ? (q_hi + kBM - 1) / kBM - jb_lo : 0;
   const int n_steps = nq * p.group;
-  const int64_t tile_base = VARLEN ? varlen_block_base(p.cu_q, zb) : 0;
+  const int64_t tile_base = VARLEN ? varlen_block_base(row_q0, zb) : 0;
   auto tile_of = [&](int hh, int jb) -> int64_t {  // workspace block of (query head, 64-query block)
     const int h = hk * p.group + hh;
     return (VARLEN ? (int64_t)h : (int64_t)zb * p.hq + h) * p.tiles_per_head + tile_base + jb;
@@ -637,9 +648,8 @@ __global__ void __launch_bounds__(256) fmha_bwd_prep_kernel(const RowParams p) {
   int row_q0 = 0, len_q = p.sq;
   int64_t base = 0;
   if constexpr (VARLEN) {
-    row_q0 = p.cu_q[zb];
-    len_q = p.cu_q[zb + 1] - row_q0;
-    base = varlen_block_base(p.cu_q, zb);
+    varlen_rows(p.cu_q, zb, p.total_q, row_q0, len_q);
+    base = varlen_block_base(row_q0, zb);
   }
   if (jb * kBM >= len_q) return;
   const int64_t tile = (VARLEN ? (int64_t)h : (int64_t)bh) * p.tiles_per_head + base + jb;
@@ -696,9 +706,8 @@ __global__ void __launch_bounds__(256) fmha_bwd_dq_kernel(const RowParams p) {
   int row_q0 = 0, len_q = p.sq;
   int64_t base = 0;
   if constexpr (VARLEN) {
-    row_q0 = p.cu_q[zb];
-    len_q = p.cu_q[zb + 1] - row_q0;
-    base = varlen_block_base(p.cu_q, zb);
+    varlen_rows(p.cu_q, zb, p.total_q, row_q0, len_q);
+    base = varlen_block_base(row_q0, zb);
   }
   if (jb * kBM >= len_q) return;
   const int64_t tile = (VARLEN ? (int64_t)h : (int64_t)bh) * p.tiles_per_head + base + jb;
@@ -1004,6 +1013,8 @@ extern "C" int gko_fmha_varlen_bwd(int dtype, int64_t b, int64_t hq, int64_t hkv
   p.dv_ss = dv_st;
   p.cu_q = cu_q;
   p.cu_k = cu_k;
+  p.total_q = (int)tq;
+  p.total_k = (int)tk;
   p.status = status;
   fmha_bwd::RowParams rp{};
   rp.hq = (int)hq;
@@ -1025,6 +1036,7 @@ extern "C" int gko_fmha_varlen_bwd(int dtype, int64_t b, int64_t hq, int64_t hkv
   rp.dq_ss = dq_st;
   rp.scale = scale;
   rp.cu_q = cu_q;
+  rp.total_q = (int)tq;
   const bool extra = softcap > 0.f || window > 0;
   const int q_blocks = (int)((max_seqlen_q + fmha_bwd::kBM - 1) / fmha_bwd::kBM);
   const int kv_tiles = (int)((max_seqlen_k + fmha_bwd::kBN - 1) / fmha_bwd::kBN);
@@ -1079,6 +1091,12 @@ extern "C" int gko_fmha_bwd_noalloc(int dtype, int64_t z, int64_t hq, int64_t hk
                                     float scale, int causal, int window, float softcap, void* dq,
                                     const int64_t* dqs, void* dk, const int64_t* dks, void* dv,
                                     const int64_t* dvs, unsigned int* status, void* stream) {
+  // the same argument checks and empty-problem return as gko_fmha_bwd, before the scratch
+  // size check and before the scratch address is looked up
+  int rc = fmha_bwd::check_common(dtype, hq, hkv, d, scale, window, softcap);
+  if (rc) return rc;
+  if (z < 0 || sq < 0 || sk < 0) return fail(GKO_ERR_INVALID, "negative attention size");
+  if (z == 0 || (sq == 0 && sk == 0)) return GKO_OK;
   const int64_t need = gko_fmha_bwd_workspace_size(z, hq, sq, d, 0);
   if (need < 0) return fail(GKO_ERR_INVALID, "fmha backward: bad sizes (z %lld, hq %lld, sq %lld, d %lld)",
                             (long long)z, (long long)hq, (long long)sq, (long long)d);

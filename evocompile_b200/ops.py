@@ -29,6 +29,32 @@ def _stream(dev):
     return ctypes.c_void_p(_lib.stream_ptr(dev))
 
 
+def _byte_range(t):
+    """[first, last) byte addresses a tensor's elements can touch (empty tensors touch none)."""
+    if t.numel() == 0:
+        return (0, 0)
+    lo = hi = t.data_ptr()
+    for size, stride in zip(t.shape, t.stride()):
+        span = (size - 1) * stride * t.element_size()
+        if span < 0:
+            lo += span
+        else:
+            hi += span
+    return (lo, hi + t.element_size())
+
+
+def _check_no_overlap(name, out, **operands):
+    """Raise if ``out`` shares memory with an operand the kernel reads while it writes ``out``:
+    epilogue stores of one CTA would race with another CTA's TMA loads of that operand."""
+    o_lo, o_hi = _byte_range(out)
+    for arg, t in operands.items():
+        if t is None:
+            continue
+        lo, hi = _byte_range(t)
+        if lo < o_hi and o_lo < hi:
+            raise RuntimeError(f"{name}: out overlaps {arg} (the GEMM would read {arg} while writing out)")
+
+
 # --------------------------------------------------------------------------- GEMM
 def addmm_act(bias, mat1, mat2, act: int = _lib.ACT_GELU, save_pre: bool = False):
     """act(mat1 @ mat2 + bias) with mat1 [..., K] and mat2 [K, N].
@@ -456,8 +482,10 @@ def fmha_bwd(q, k, v, attn_bias, out, lse, dout, scale=None, causal=0, window=0,
 
 def fmha_varlen_bwd(q, k, v, out, lse, dout, cu_seqlens_q, cu_seqlens_k, max_seqlen_q, max_seqlen_k, scale=None,
                     causal=0, window=0, softcap=0.0):
-    """Backward of ``fmha_varlen_fwd`` -> (dq [tq, hq, d], dk, dv [tk, hkv, d]). The kernels trust
-    cu_seqlens: they must be non-decreasing from 0 to the token counts, as for the forward."""
+    """Backward of ``fmha_varlen_fwd`` -> (dq [tq, hq, d], dk, dv [tk, hkv, d]). cu_seqlens must be
+    non-decreasing from 0 to the token counts, as for the forward; the kernels clamp every
+    sequence's rows to [0, tq) / [0, tk), so malformed cu_seqlens give wrong gradients but no
+    access outside the tensors and the workspace."""
     dev = _lib.require_cuda(q, k, v, out, lse, dout, cu_seqlens_q, cu_seqlens_k)
     if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
         raise RuntimeError("fmha_varlen_bwd: q, k, v must be 3-D [tokens, heads, d]")
@@ -540,8 +568,11 @@ def linear_residual(x, weight, resid, out=None):
     """x @ weight^T + resid with the residual add in the GEMM epilogue (gko_linear_residual).
 
     x [m, k] and weight [n, k] row-major, resid [m, n]; bf16 / f16. ``out`` (default: a new
-    tensor) may be ``resid`` itself for an in-place residual update. Returns out.
+    tensor) may be ``resid`` itself for an in-place residual update, but must not overlap
+    x or weight. Returns out.
     """
+    if out is not None:
+        _check_no_overlap("linear_residual", out, x=x, weight=weight)
     dev = _lib.require_cuda(x, weight, resid, out)
     if x.dim() != 2 or weight.dim() != 2 or resid.dim() != 2:
         raise RuntimeError("linear_residual: x [m, k], weight [n, k], resid [m, n]")

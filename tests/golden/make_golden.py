@@ -120,4 +120,8 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("EVOCOMPILE_REF", "/root/reference/EvoCompile"))
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("EVOCOMPILE_REF")
+    if not root:
+        sys.exit("usage: python tests/golden/make_golden.py <EvoCompile checkout root> "
+                 "(or set EVOCOMPILE_REF); the root holds eval/kernels")
+    main(root)

@@ -211,3 +211,23 @@ def test_pass_install_idempotent_and_composed():
     assert calls == [1, 2]
     with pytest.raises(TypeError):
         pass_install.install_inductor_pass("pre_grad_custom_pass", 3)
+
+
+def test_linear_residual_rejects_out_overlapping_operands():
+    """out may be the residual (in-place update) but never x or the weight: the epilogue's stores
+    would race with other CTAs' loads of them. Checked before any device work, so CPU tensors
+    reach the check."""
+    from evocompile_b200 import ops
+
+    buf = torch.zeros(64, 64, dtype=torch.bfloat16)
+    x, w = buf[:32], torch.zeros(32, 64, dtype=torch.bfloat16)
+    resid = torch.zeros(32, 32, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="overlaps x"):
+        ops.linear_residual(x, w, resid, out=buf[16:48, :32])
+    with pytest.raises(RuntimeError, match="overlaps weight"):
+        ops.linear_residual(x, w, resid, out=w[:, :32])
+    # disjoint rows of the same buffer and the residual itself pass the check (then the CPU check refuses)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.linear_residual(x, w, resid, out=buf[32:, :32])
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.linear_residual(x, w, resid, out=resid)

@@ -181,3 +181,50 @@ def test_bwd_full_config_sampled_heads():
         (p @ vs).backward(do[b, h].float())
         for g, r in ((dq[b, h], qs.grad), (dk[b, h], ks.grad), (dv[b, h], vs.grad)):
             assert oracle.rel_err(g, r) <= TOL
+
+
+@pytest.mark.parametrize("causal", [0, 1])
+def test_bwd_varlen_edges_write_nothing_outside(causal):
+    """Valid edge cases of cu_seqlens (empty and one-token sequences, the last sequence ending
+    exactly at the packed token count): dq, dk, dv and the workspace are the heads of larger
+    buffers whose tails hold a canary; the kernels write only inside the tensors."""
+    import ctypes
+
+    lens = [0, 1, 1, 64, 0, 130, 1, 200]
+    hq, hkv, d = 4, 2, 128
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    t = int(cu[-1])
+    g = torch.Generator().manual_seed(71 + causal)
+    q = torch.randn(t, hq, d, generator=g).to(torch.bfloat16)
+    k = torch.randn(t, hkv, d, generator=g).to(torch.bfloat16)
+    v = torch.randn(t, hkv, d, generator=g).to(torch.bfloat16)
+    do = torch.randn(t, hq, d, generator=g).to(torch.bfloat16)
+    ref = oracle.attention_varlen_bwd(q, k, v, do, cu, cu, d ** -0.5, causal)
+    cud = cu.cuda()
+    qd, kd, vd, dod = q.cuda(), k.cuda(), v.cuda(), do.cuda()
+    out, lse = ops.fmha_varlen_fwd(qd, kd, vd, cud, cud, max(lens), max(lens), d ** -0.5, causal)
+    canary = 7.0
+    tail = 4096
+    bq = torch.full((t * hq * d + tail,), canary, dtype=torch.bfloat16, device="cuda")
+    bk = torch.full((t * hkv * d + tail,), canary, dtype=torch.bfloat16, device="cuda")
+    bv = torch.full((t * hkv * d + tail,), canary, dtype=torch.bfloat16, device="cuda")
+    dq, dk, dv = bq[: t * hq * d].view(t, hq, d), bk[: t * hkv * d].view(t, hkv, d), bv[: t * hkv * d].view(t, hkv, d)
+    lib = _lib.load()
+    ws_bytes = lib.gko_fmha_bwd_workspace_size(len(lens), hq, t, d, 1)
+    wsb = torch.full((ws_bytes // 4 + tail,), canary, dtype=torch.float32, device="cuda")
+    vp = lambda x: ctypes.c_void_p(x.data_ptr())  # noqa: E731
+    dev = torch.device("cuda", 0)
+    rc = lib.gko_fmha_varlen_bwd(
+        _lib.dtype_code(q.dtype), len(lens), hq, hkv, d, t, t, max(lens), max(lens),
+        vp(qd), qd.stride(0), qd.stride(1), vp(kd), kd.stride(0), kd.stride(1), vp(vd), vd.stride(0), vd.stride(1),
+        vp(out), out.stride(0), out.stride(1), vp(dod), dod.stride(0), dod.stride(1), vp(lse), vp(cud), vp(cud),
+        float(d ** -0.5), causal, 0, 0.0, vp(dq), dq.stride(0), dq.stride(1), vp(dk), dk.stride(0), dk.stride(1),
+        vp(dv), dv.stride(0), dv.stride(1), vp(wsb), ws_bytes,
+        ctypes.c_void_p(_lib.status_word(dev).data_ptr()), ctypes.c_void_p(_lib.stream_ptr(dev)))
+    _lib.check(rc, "gko_fmha_varlen_bwd")
+    torch.cuda.synchronize()
+    assert _lib.read_status(dev) == 0
+    _check((dq, dk, dv), ref)
+    for buf, n in ((bq, t * hq * d), (bk, t * hkv * d), (bv, t * hkv * d)):
+        assert (buf[n:] == canary).all()
+    assert (wsb[ws_bytes // 4:] == canary).all()

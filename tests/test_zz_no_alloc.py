@@ -28,8 +28,9 @@ def _vp(t):
     return ctypes.c_void_p(t.data_ptr() if t is not None else 0)
 
 
-def _noalloc(q, k, v, out, lse, dout, scale, causal):
-    z, hq, sq, d = q.shape
+def _noalloc(q, k, v, out, lse, dout, scale, causal, d=None):
+    z, hq, sq, d_ = q.shape
+    d = d_ if d is None else d
     hkv, sk = k.shape[1], k.shape[2]
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     dev = q.device
@@ -74,3 +75,12 @@ def test_noalloc_rejects_problems_beyond_the_scratch():
     lse = torch.zeros(z * hq, s, dtype=torch.float32, device="cuda")
     with pytest.raises(RuntimeError, match="scratch"):
         _noalloc(t, t, t, t, lse, t, 0.1, 1)
+
+
+def test_noalloc_argument_errors_match_workspace_entry_point():
+    """A head dim the kernels do not implement is refused with the same error as gko_fmha_bwd
+    (the head-dim rule), before the scratch size is computed."""
+    t = torch.zeros(1, 2, 64, 128, dtype=torch.bfloat16, device="cuda")
+    lse = torch.zeros(2, 64, dtype=torch.float32, device="cuda")
+    with pytest.raises(RuntimeError, match="head dim 64 or 128"):
+        _noalloc(t, t, t, t, lse, t, 0.1, 1, d=96)
