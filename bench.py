@@ -170,6 +170,11 @@ def max_over_ranks(v, world):
 class SwigluMLP:
     name = "swiglu"
     dominant = "swiglu_gateup"
+    last_out = None  # the result of the last timed step
+
+    def close(self):
+        """Release this workload's device memory before the next one is built."""
+        self.__dict__.clear()
 
     def __init__(self, dev, world, rank):
         from evocompile_b200 import ops
@@ -505,7 +510,20 @@ class FmhaVarlen(SwigluMLP):
                                                               128 ** -0.5, 1)[0])
 
     def torch_reference(self):
-        return None, None
+        """Per-sequence causal GQA SDPA over the packed tensors (torch has no varlen SDPA API)."""
+        import torch.nn.functional as F
+
+        bounds = list(zip(self.cu.tolist()[:-1], self.cu.tolist()[1:]))
+
+        def ref(q, k, v):
+            outs = []
+            for s, e in bounds:
+                qs, ks, vs = (t[s:e].transpose(0, 1)[None] for t in (q, k, v))
+                outs.append(F.scaled_dot_product_attention(qs, ks, vs, is_causal=True, enable_gqa=True)[0]
+                            .transpose(0, 1))
+            return torch.cat(outs)
+
+        return ref, (self.q, self.k, self.v)
 
     def cpu_sample(self):
         import oracle
@@ -533,8 +551,11 @@ class TPBlockWorkload(SwigluMLP):
         self.cfg = BlockConfig()
         self.B, self.S = 4, 4096
         self.world = world
+        self.rank = rank
         full = init_weights(self.cfg, dev, torch.bfloat16, seed=7)
         self.full = full if world == 1 else None
+        # rank 0 keeps an fp32 host copy of the full weights for the CPU leg (oracle timing and parity)
+        self.w_host = {k: v.float().cpu() for k, v in full.items()} if rank == 0 else None
         group = None
         if world > 1:
             import torch.distributed as dist
@@ -566,6 +587,63 @@ class TPBlockWorkload(SwigluMLP):
     def step(self, ev=None):
         # the events bracket the fused gate/up + SwiGLU kernel inside the block
         return self.block.forward(self.x, events=ev)
+
+    def phases(self, steps, world):
+        """Device ms per step of each phase of the block (CUDA events at every phase boundary on
+        the launching stream, averaged over ``steps`` steps, max over ranks). With NCCL the
+        row-parallel projections split into their GEMM and their all-reduce."""
+        marks = []
+
+        def mark(name):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            marks.append((name, e))
+
+        for _ in range(steps):
+            self.block.forward(self.x, mark=mark)
+        torch.cuda.synchronize()
+        # an interval that ends at a projection's mark and starts at that GEMM's own mark is its all-reduce
+        out = {}
+        names = [n for n, _ in marks]
+        for i in range(1, len(marks)):
+            name, prev = names[i], names[i - 1]
+            if name == "start":
+                continue
+            key = f"{name}_allreduce" if prev == f"{name}_gemm" else name
+            out[key] = out.get(key, 0.0) + marks[i - 1][1].elapsed_time(marks[i][1])
+        keys = sorted(out)
+        vals = [out[k] / steps for k in keys]
+        if world > 1:
+            import torch.distributed as dist
+
+            t = torch.tensor(vals, dtype=torch.float64, device=self.x.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            vals = t.tolist()
+        return dict(zip(keys, vals))
+
+    def cpu_check(self):
+        """Parity of this run's output (the last timed step, rank 0) against the oracle on the
+        first 512 tokens of sequence 0: rows of a causal block depend only on their prefix, so
+        the oracle's 512-token block gives exactly those rows. Reported as max|err| / max|ref| of
+        the block output and of the block's update (output - x)."""
+        import oracle
+
+        torch.set_num_threads(os.cpu_count() or 1)
+        P = 512
+        xs = self.x[:1, :P].float().cpu()
+        t0 = time.perf_counter()
+        ref = oracle.llama_block(xs, self.w_host, self.cfg)
+        dt = time.perf_counter() - t0
+        got = self.last_out[:1, :P].float().cpu()
+        rel = ((got - ref).abs().max() / ref.abs().max()).item()
+        d_got, d_ref = got - xs, ref - xs
+        rel_d = ((d_got - d_ref).abs().max() / d_ref.abs().max()).item()
+        return {"parity": {"rel_err": rel, "rel_err_delta": rel_d, "tol": 2e-2, "ok": rel <= 2e-2,
+                           "rows": f"sequence 0, tokens [0, {P}) of the timed run's output (rank 0)",
+                           "oracle": "oracle.llama_block, fp32 on the host cores, from the same bf16 weights",
+                           "oracle_s": dt},
+                "comm": self.block.comm if self.world > 1 else "none",
+                "nccl": {"backend": "nccl", "ranks": self.world} if self.world > 1 else None}
 
     def e2e_setup(self):
         return [self.x.cpu().pin_memory()], (lambda d: self.block.forward(d[0]))
@@ -606,10 +684,8 @@ class TPBlockWorkload(SwigluMLP):
 
     def cpu_sample(self):
         import oracle
-        from evocompile_b200.block import init_weights
 
-        cfg = self.cfg
-        w = init_weights(cfg, torch.device("cpu"), torch.float32, seed=7)
+        cfg, w = self.cfg, self.w_host
         xs = self.x[:1, :512].float().cpu()
         return (lambda: oracle.llama_block(xs, w, cfg)), cfg.flops(512, 512), \
             "one 512-token sequence through the full-width block (fp32 oracle)"
@@ -714,6 +790,184 @@ def run_reference(args):
     return 0
 
 
+def _warm(step, warmup, world, dev, min_s=1.0):
+    """W warm-up steps, then more until about ``min_s`` seconds of work have run (after a stretch
+    of host-only work the GPU's clocks take a while to come back up). Every rank runs the same
+    count: a step of the tensor-parallel block holds collectives."""
+    t0 = time.perf_counter()
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    per_step = (time.perf_counter() - t0) / max(1, warmup)
+    more = int(max_over_ranks(max(0.0, min_s - per_step * warmup) / max(per_step, 1e-6), world))
+    for _ in range(more):
+        step()
+    torch.cuda.synchronize(dev)
+
+
+def _timed_region(wl, steps, warmup, world, local, dev):
+    """W warm-up steps, then K steps between barrier + synchronize, CUDA events on the launching
+    stream; per-step events bracket the dominant kernel. Returns max-over-ranks step and kernel ms."""
+    from evocompile_b200 import _lib
+
+    stream = torch.cuda.current_stream(dev)
+    _warm(wl.step, warmup, world, dev)
+    if _lib.read_status(dev):
+        raise RuntimeError(f"{wl.name}: kernel timeout during warm-up")
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for i in range(steps):
+            wl.last_out = wl.step(kev[i])
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    kern_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in kev) / steps, world)
+    return ms, kern_ms, clocks.summary(), _lib.read_status(dev)
+
+
+def _e2e_record(wl, steps, warmup, world, dev, scale):
+    """End to end through the public op API, pinned host memory to pinned host memory."""
+    host, fn = wl.e2e_setup()
+    pipe = E2EPipeline(host, fn, dev)
+    stream = torch.cuda.current_stream(dev)
+    n = max(5, min(steps, 50))
+    # warm-up: untimed pipelined steps for at least a second and at least the timed count (the
+    # first pipelined host copies of a process run well below the link's rate for a while)
+    counter = iter(range(1 << 30))
+    _warm(lambda: pipe.step(next(counter)), max(2, warmup, n), world, dev)
+    pipe.join()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    pipe.begin(a)
+    for i in range(n):
+        pipe.step(i)
+    pipe.join()
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    local_ms = a.elapsed_time(b) / n
+    pipe_ms = max_over_ranks(local_ms, world)
+    h2d, d2h = pipe.h2d_bytes, pipe.d2h_bytes
+    del pipe, host, fn
+    return {"value": scale * wl.flop_step / (pipe_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": pipe_ms, "steps": n,
+            # this rank's host link rate over the pipelined steps: at N > 1 all ranks share one
+            # host's PCIe / memory bandwidth, which bounds e2e before any kernel does
+            "h2d_gbs_per_rank": h2d / (local_ms / 1e3) / 1e9, "d2h_gbs_per_rank": d2h / (local_ms / 1e3) / 1e9}
+
+
+def _comparators(wl, steps, dev):
+    """torch eager and torch.compile of the harness-equivalent module on the same GPU, timed like
+    our arm (K steps, CUDA events), two alternating rounds with our step repeated between them;
+    best round per arm."""
+    stream = torch.cuda.current_stream(dev)
+    comparators = {}
+    fn, fargs = wl.torch_reference()
+    arms = {}
+    if fn is not None:
+        arms["torch_eager"] = lambda: fn(*fargs)
+        if getattr(wl, "compile_comparator", True):
+            try:
+                cfn = torch.compile(fn)
+                arms["torch_compile"] = lambda: cfn(*fargs)
+            except Exception as e:  # noqa: BLE001
+                comparators["torch_compile"] = {"error": repr(e)[:200]}
+    arms["gko_repeat"] = lambda: wl.step()
+    if hasattr(wl, "extra_arms"):
+        arms.update(wl.extra_arms())
+    best = {}
+    for name, f in list(arms.items()):
+        try:
+            for _ in range(3):
+                f()
+            torch.cuda.synchronize(dev)
+        except Exception as e:  # noqa: BLE001
+            comparators[name] = {"error": repr(e)[:200]}
+            arms.pop(name)
+    for _ in range(2):
+        for name, f in arms.items():
+            x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            x0.record(stream)
+            for _ in range(steps):
+                f()
+            x1.record(stream)
+            torch.cuda.synchronize(dev)
+            t = x0.elapsed_time(x1) / steps
+            best[name] = min(best.get(name, t), t)
+    for name, t in best.items():
+        comparators[name] = {"ms_per_step": t, "tflops": wl.flop_step / t / 1e9}
+    torch._dynamo.reset()
+    return comparators
+
+
+def _cpu_leg(wl, budget_s):
+    """The oracle on a bounded sample of the workload on the host cores (rank 0): the CPU
+    baseline, and for workloads that define ``cpu_check`` the parity of the GPU result."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    fn, flops, sample = wl.cpu_sample()
+    tf, dt, reps = time_cpu(fn, flops, budget_s=budget_s)
+    cpu = {"value": tf, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+           "sample": f"{sample}; {reps} reps, {dt * 1e3:.1f} ms each"}
+    return cpu
+
+
+def measure(wl, args, world, rank, local, dev, compare, cpu, cpu_budget_s=10.0):
+    """Every figure of one workload's record (identical collective sequence on every rank)."""
+    from evocompile_b200 import _lib
+
+    ms, kern_ms, clocks, status = _timed_region(wl, args.steps, args.warmup, world, local, dev)
+    extra = {}
+    if hasattr(wl, "phases"):
+        extra["phases_ms"] = wl.phases(args.steps, world)
+    scale = 1 if getattr(wl, "scaling", "weak") == "strong" else world  # strong: flop_step is the whole job
+    e2e = _e2e_record(wl, args.steps, args.warmup, world, dev, scale)
+    comparators = _comparators(wl, args.steps, dev) if (world == 1 and compare) else None
+    cpu_rec = None
+    if rank == 0 and hasattr(wl, "cpu_check"):
+        extra.update(wl.cpu_check())
+    if rank == 0 and world == 1 and cpu:
+        cpu_rec = _cpu_leg(wl, cpu_budget_s)
+    status |= _lib.read_status(dev)
+    pk, pk_src = peaks()
+    peak = pk["bf16_tflops"]
+    value = scale * wl.flop_step / (ms / 1e3) / 1e12
+    achieved = wl.flop_gateup / (kern_ms / 1e3) / 1e12
+    traffic = traffic_per_launch(getattr(wl, "traffic_key", wl.dominant))
+    rec = {
+        "value": value, "unit": "TFLOP/s", "ms_per_step": ms, "n_gpus": world,
+        "scaling": getattr(wl, "scaling", "weak"), "config": wl.config,
+        "pct_of_peak": value / (world * peak),
+        "tokens_per_s": (wl.B * wl.S / (ms / 1e3)) if getattr(wl, "scaling", "weak") == "strong"
+        else (world * wl.T / (ms / 1e3) if hasattr(wl, "T") else None),
+        "roofline": {"bound": "tensor", "kernel": wl.dominant, "achieved": achieved, "peak": peak,
+                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                     "peak_source": f"{pk_src} bf16 burst (MEASURED_PEAKS.json)" if pk_src == "measured"
+                     else "fallback 1590 TFLOP/s", "flop_per_launch": wl.flop_gateup,
+                     "avg_launch_ms": kern_ms},
+        "cpu_baseline": cpu_rec,
+        "e2e": e2e,
+        "gpu_launches": wl.launches_per_step * args.steps,
+        "clocks": clocks,
+        "comparators": comparators,
+        "kernel_status": status,
+    }
+    rec.update(extra)
+    return rec
+
+
+# the per-configuration records added to the default line: every configuration of the
+# operators at its full size (sharded at N > 1 as the configuration shards)
+SUB_WORKLOADS = ("addmm_gelu", "fmha_causal", "fmha_varlen", "fmha_bwd", "tp_block")
+
+
 def run_ours(args):
     world, rank, local = dist_setup()
     if world != args.gpus and rank == 0:
@@ -723,129 +977,40 @@ def run_ours(args):
     from evocompile_b200 import _lib
 
     _lib.load()
+    compare = not args.no_compare
     wl = WORKLOADS[args.workload](dev, world, rank)
-    stream = torch.cuda.current_stream(dev)
+    rec = measure(wl, args, world, rank, local, dev, compare, not args.no_cpu)
+    del wl
+    torch.cuda.empty_cache()
 
-    for _ in range(args.warmup):
-        wl.step()
-    torch.cuda.synchronize(dev)
-    assert _lib.read_status(dev) == 0, "kernel timeout during warm-up"
-
-    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize(dev)
-    with ClockSampler(local) as clocks:
-        e0.record(stream)
-        for i in range(args.steps):
-            wl.step(kev[i])
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-    barrier(world)
-    ms_local = e0.elapsed_time(e1) / args.steps
-    kern_ms_local = sum(a.elapsed_time(b) for a, b in kev) / args.steps
-    ms = max_over_ranks(ms_local, world)
-    kern_ms = max_over_ranks(kern_ms_local, world)
-    status = _lib.read_status(dev)
-
-    # end to end through the public op API, pinned host memory to pinned host memory
-    pipe = E2EPipeline(*wl.e2e_setup(), dev)
-    for i in range(max(2, args.warmup)):
-        pipe.step(i)
-    pipe.join()
-    torch.cuda.synchronize(dev)
-    h2d, d2h = pipe.h2d_bytes, pipe.d2h_bytes
-    e2e_steps = max(5, min(args.steps, 50))
-    barrier(world)
-    torch.cuda.synchronize(dev)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    pipe.begin(a)
-    for i in range(e2e_steps):
-        pipe.step(i)
-    pipe.join()
-    b.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier(world)
-    e2e_ms = max_over_ranks(a.elapsed_time(b) / e2e_steps, world)
-
-    # comparators on the same GPU (N = 1 only): torch eager and torch.compile of the
-    # harness-equivalent module, timed like our arm (K steps, CUDA events), two
-    # alternating rounds with our step repeated between them; best round per arm.
-    comparators = {}
-    if world == 1 and not args.no_compare:
-        fn, fargs = wl.torch_reference()
-        arms = {}
-        if fn is not None:
-            arms["torch_eager"] = lambda: fn(*fargs)
-            if getattr(wl, "compile_comparator", True):
-                try:
-                    cfn = torch.compile(fn)
-                    arms["torch_compile"] = lambda: cfn(*fargs)
-                except Exception as e:  # noqa: BLE001
-                    comparators["torch_compile"] = {"error": repr(e)[:200]}
-        arms["gko_repeat"] = lambda: wl.step()
-        if hasattr(wl, "extra_arms"):
-            arms.update(wl.extra_arms())
-        best = {}
-        for name, f in list(arms.items()):
-            try:
-                for _ in range(3):
-                    f()
-                torch.cuda.synchronize(dev)
-            except Exception as e:  # noqa: BLE001
-                comparators[name] = {"error": repr(e)[:200]}
-                arms.pop(name)
-        for _ in range(2):
-            for name, f in arms.items():
-                x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                x0.record(stream)
-                for _ in range(args.steps):
-                    f()
-                x1.record(stream)
-                torch.cuda.synchronize(dev)
-                t = x0.elapsed_time(x1) / args.steps
-                best[name] = min(best.get(name, t), t)
-        for name, t in best.items():
-            comparators[name] = {"ms_per_step": t, "tflops": wl.flop_step / t / 1e9}
-
-    cpu = None
-    if world == 1 and rank == 0 and not args.no_cpu:
-        torch.set_num_threads(os.cpu_count() or 1)
-        fn, flops, sample = wl.cpu_sample()
-        tf, dt, reps = time_cpu(fn, flops)
-        cpu = {"value": tf, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
-               "sample": f"{sample}; {reps} reps, {dt * 1e3:.1f} ms each"}
+    subs = {}
+    names = [] if args.no_workloads or args.workload != "swiglu" else \
+        [n for n in (args.workloads.split(",") if args.workloads else SUB_WORKLOADS) if n]
+    for name in names:
+        sub = WORKLOADS[name](dev, world, rank)
+        try:
+            subs[name] = measure(sub, args, world, rank, local, dev, compare, not args.no_cpu, cpu_budget_s=5.0)
+        finally:
+            sub.close()
+            del sub
+            torch.cuda.empty_cache()
 
     if rank == 0:
-        pk, pk_src = peaks()
-        peak = pk["bf16_tflops"]
-        scale = 1 if getattr(wl, "scaling", "weak") == "strong" else world  # strong: flop_step is the whole job
-        value = scale * wl.flop_step / (ms / 1e3) / 1e12
-        achieved = wl.flop_gateup / (kern_ms / 1e3) / 1e12
-        # DRAM bytes of a capture of this exact kernel and shape, or null when none is committed
-        traffic = traffic_per_launch(getattr(wl, "traffic_key", wl.dominant))
         line = {
-            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": getattr(wl, "scaling", "weak"),
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": wl.config,
-            "pct_of_peak": value / (world * peak),
-            "tokens_per_s": (wl.B * wl.S / (ms / 1e3)) if getattr(wl, "scaling", "weak") == "strong"
-            else (world * wl.T / (ms / 1e3) if hasattr(wl, "T") else None),
-            "roofline": {"bound": "tensor", "kernel": wl.dominant, "achieved": achieved, "peak": peak,
-                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": f"{pk_src} bf16 burst (MEASURED_PEAKS.json)" if pk_src == "measured"
-                         else "fallback 1590 TFLOP/s", "flop_per_launch": wl.flop_gateup,
-                         "avg_launch_ms": kern_ms},
-            "cpu_baseline": cpu,
-            "e2e": {"value": scale * wl.flop_step / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-            "gpu_launches": wl.launches_per_step * args.steps,
-            "clocks": clocks.summary(),
-            "comparators": comparators or None,
-            "kernel_status": status,
+            "metric": METRIC, "value": rec["value"], "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": rec["ms_per_step"], "higher_is_better": True,
+            "scaling": rec["scaling"], "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": rec["config"],
         }
+        for key in ("pct_of_peak", "tokens_per_s", "roofline", "cpu_baseline", "e2e", "gpu_launches", "clocks",
+                    "comparators", "kernel_status", "phases_ms", "rel_err", "rel_err_delta", "parity", "comm",
+                    "nccl"):
+            if key in rec:
+                line[key] = rec[key]
+        if subs:
+            for r in subs.values():
+                r.pop("n_gpus", None)
+            line["workloads"] = subs
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -863,6 +1028,10 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="swiglu")
     ap.add_argument("--no-compare", action="store_true", help="skip the torch eager / torch.compile comparators")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-workloads", action="store_true",
+                    help="default line without the per-configuration records (headline only)")
+    ap.add_argument("--workloads", default="",
+                    help=f"comma-separated per-configuration records to add (default: {','.join(SUB_WORKLOADS)})")
     ap.add_argument("--small", action="store_true",
                     help="attention workloads at B=4, H=16 (a capture-sized case for ncu --set full)")
     ap.add_argument("--tp-comm", choices=("auto", "fused", "nccl"), default="auto",

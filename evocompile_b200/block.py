@@ -20,9 +20,9 @@ on rank 0 before the all-reduce. With
 ``comm="fused"`` the two row-parallel projections reduce their outputs across the group
 inside the GEMM over NVLink (``evocompile_b200.tp.FusedAllReduceLinear``); ``comm="nccl"``
 runs the GEMM and then an NCCL all-reduce. ``comm="auto"`` (the default) picks the fused
-form on two ranks and NCCL on more: on B200 the fused form was faster at TP2 (2437 vs 2378
-TFLOP/s on the B=4 S=4096 block) and slower at TP4 (3942 vs 4234), where each rank's GEMM
-shrinks to a quarter while its NVLink reduction traffic stays the full output.
+form on two ranks and NCCL on more: with the fused form each rank's GEMM shrinks with the rank
+count while its NVLink reduction traffic stays the whole output, so its reductions stop hiding
+behind the GEMM's main loop as the rank count grows.
 """
 
 from __future__ import annotations
@@ -127,9 +127,10 @@ class TPBlock:
         self.comm = comm
         self._fused = {}
 
-    def _row_parallel(self, x, weight, slot, resid=None):
+    def _row_parallel(self, x, weight, slot, resid=None, mark=None):
         """x @ weight^T summed over the group (row-parallel projection), plus ``resid`` (replicated
-        on every rank, updated in place) when given."""
+        on every rank, updated in place) when given. ``mark(name)``, if given, is called between
+        the GEMM and the NCCL all-reduce (the fused form has no such boundary)."""
         if self.world == 1:
             if resid is not None:
                 return ops.linear_residual(x, weight, resid, out=resid)
@@ -140,6 +141,8 @@ class TPBlock:
                 y = ops.linear_residual(x, weight, resid, out=resid)
             else:
                 y = ops.linear(x, weight)
+            if mark is not None:
+                mark(f"{('o_proj', 'down')[slot]}_gemm")
             torch.distributed.all_reduce(y, op=torch.distributed.ReduceOp.SUM, group=self.group)
             return y
         from .tp import FusedAllReduceLinear
@@ -152,13 +155,19 @@ class TPBlock:
         y = f(x, weight)
         return y if resid is None else resid.add_(y)
 
-    def forward(self, x: torch.Tensor, events=None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, events=None, mark=None) -> torch.Tensor:
         """x [B, S, d_model] (bf16) -> [B, S, d_model]. ``events`` (start, end) CUDA events, if
-        given, bracket the fused gate/up kernel (for per-kernel timing)."""
+        given, bracket the fused gate/up kernel (for per-kernel timing). ``mark(name)``, if given,
+        is called at each phase boundary on the launching stream (``start``, ``qkv``, ``attention``,
+        ``o_proj``, ``norm2``, ``gate_up``, ``down``; with NCCL also ``o_proj_gemm`` and
+        ``down_gemm`` between each GEMM and its all-reduce), so a caller can record a CUDA event
+        per boundary and time each phase."""
         cfg, w = self.cfg, self.w
         B, S, d = x.shape
         T, hd = B * S, cfg.head_dim
         hq, hkv = w["hq_local"], w["hkv_local"]
+        mk = mark if mark is not None else (lambda name: None)
+        mk("start")
         x2 = x.reshape(T, d)
         inv1 = ops.rms_stats(x2, cfg.eps)                                 # 1/rms per token (fp32)
         qkv = ops.linear_rowscale(x2, w["wqkv_n"], inv1)                  # rmsnorm(x) Wqkv^T  [T, (hq + 2 hkv) * D]
@@ -167,15 +176,22 @@ class TPBlock:
         v = qkv[:, (hq + hkv) * hd:].view(T, hkv, hd)
         # q and k heads are adjacent in each qkv row: one RoPE launch covers both
         ops.rope_(qkv[:, : (hq + hkv) * hd].view(T, hq + hkv, hd), cfg.rope_theta, seq_len=S)
+        mk("qkv")
         as4 = lambda t: t.view(B, S, t.shape[1], hd).transpose(1, 2)     # noqa: E731  [B, H, S, D] views
         attn = torch.empty(T, hq, hd, device=x.device, dtype=x.dtype)
         ops.fmha_fwd(as4(q), as4(k), as4(v), None, hd ** -0.5, 1, out=as4(attn))
-        o = self._row_parallel(attn.view(T, hq * hd), w["wo"], 0)          # row-parallel partial -> sum
+        mk("attention")
+        o = self._row_parallel(attn.view(T, hq * hd), w["wo"], 0, mark=mark)  # row-parallel partial -> sum
+        mk("o_proj")
         inv2, x1 = ops.rms_stats(o, cfg.eps, residual=x2)               # x1 = x + o, 1/rms(x1)
+        mk("norm2")
         if events is not None:
             events[0].record()
         g = ops.linear_rowscale(x1, w["w_gate_up_n"], inv2, swiglu=True)  # SwiGLU(rmsnorm(x1) W^T) [T, ff_local]
         if events is not None:
             events[1].record()
+        mk("gate_up")
         # down projection + residual (in the GEMM epilogue on one rank, and on rank 0 with NCCL)
-        return self._row_parallel(g, w["w_down"], 1, resid=x1).view(B, S, d)
+        y = self._row_parallel(g, w["w_down"], 1, resid=x1, mark=mark).view(B, S, d)
+        mk("down")
+        return y
