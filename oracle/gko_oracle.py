@@ -258,7 +258,12 @@ def llama_block(x, w, cfg):
     pos = torch.arange(S)
     q = torch.stack([rope(q[b], cfg.rope_theta, pos) for b in range(B)])
     k = torch.stack([rope(k[b], cfg.rope_theta, pos) for b in range(B)])
-    o, _ = attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), None, hd ** -0.5, 1)
+    # attention one kv group at a time (its query heads against its one kv head): the same math,
+    # with the [B, heads, S, S] logits held for one group only
+    g = cfg.n_heads // cfg.n_kv_heads
+    qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    o = torch.cat([attention(qh[:, j * g:(j + 1) * g], kh[:, j:j + 1], vh[:, j:j + 1], None, hd ** -0.5, 1)[0]
+                   for j in range(cfg.n_kv_heads)], dim=1)
     o = F.linear(o.transpose(1, 2).reshape(B, S, cfg.n_heads * hd), _f32(w["wo"]))
     x1 = xf + o
     h2 = rmsnorm(x1, w["mlp_norm"], cfg.eps)

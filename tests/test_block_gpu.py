@@ -229,3 +229,10 @@ def test_fused_allreduce_linear_2gpu(use_multicast):
         assert isinstance(errs[i + 1], float), errs
         assert errs[i] <= TOL, errs
         assert errs[i + 1] == 0.0, "a kernel reported a timeout"
+
+
+@pytest.mark.slow
+def test_block_full_width_full_sequence():
+    """Llama-3-70B widths on one full 4096-token sequence: RoPE positions and the causal range
+    reach the configuration's whole length (the fp32 oracle runs on the host cores)."""
+    assert _block_check(BlockConfig(), 1, 4096) <= TOL

@@ -163,3 +163,37 @@ def test_fmha_full_config_sampled_heads():
                                   v[b:b + 1, h:h + 1].cpu(), None, D ** -0.5, 1)
         assert oracle.rel_err(out[b:b + 1, h:h + 1], ro) <= TOL
         assert (lse.view(B, H, S)[b, h].cpu() - rl.view(S)).abs().max().item() <= 2e-2
+
+
+@pytest.mark.slow
+def test_fmha_varlen_full_config():
+    """The benchmarked GQA varlen configuration exactly: 16 sequences with lengths drawn by
+    randint(512, 8193) from seed 0, Hq=64, Hkv=8, D=128, causal. The fp32 oracle checks every
+    head of the shortest and the longest sequence and four more (sequence, head) pairs."""
+    gl = torch.Generator().manual_seed(0)
+    lens = torch.randint(512, 8193, (16,), generator=gl).tolist()
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    t = int(cu[-1])
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(4000)
+    q = torch.randn(t, 64, 128, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(t, 8, 128, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(t, 8, 128, device=dev, generator=g).to(torch.bfloat16)
+    cud = cu.to(dev)
+    out, lse = ops.fmha_varlen_fwd(q, k, v, cud, cud, max(lens), max(lens), 128 ** -0.5, 1)
+    torch.cuda.synchronize()
+    assert _lib.read_status(dev) == 0
+    short, long_ = min(range(16), key=lambda i: lens[i]), max(range(16), key=lambda i: lens[i])
+    pairs = [(short, h) for h in range(64)] + [(long_, h) for h in range(64)]
+    rnd = torch.Generator().manual_seed(1)
+    pairs += [(int(torch.randint(16, (1,), generator=rnd)), int(torch.randint(64, (1,), generator=rnd)))
+              for _ in range(4)]
+    for sq, h in pairs:
+        a, b = int(cu[sq]), int(cu[sq + 1])
+        hk = h // 8
+        qs = q[a:b, h].cpu()[None, None]
+        ks = k[a:b, hk].cpu()[None, None]
+        vs = v[a:b, hk].cpu()[None, None]
+        ro, rl = oracle.attention(qs, ks, vs, None, 128 ** -0.5, 1)
+        assert oracle.rel_err(out[a:b, h], ro[0, 0]) <= TOL, (sq, h)
+        assert (lse[h, a:b].cpu() - rl.view(-1)).abs().max().item() <= 2e-2, (sq, h)
