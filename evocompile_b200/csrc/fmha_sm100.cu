@@ -56,12 +56,6 @@ constexpr int kKStages = GKO_FMHA_K_STAGES;
 #ifndef GKO_FMHA_LATE_KWAIT
 #define GKO_FMHA_LATE_KWAIT 1
 #endif
-// In tiles without masked keys, pair c of each 8 uses the FMA-pipe exponential when
-// bit (c % 8) is set, the MUFU otherwise (a knob for balancing the two pipes).
-#ifndef GKO_FMHA_POLY_PAIRS
-#define GKO_FMHA_POLY_PAIRS 0x00u  // measured fastest on B200: all exponentials on MUFU
-#endif
-constexpr uint32_t kPolyPairs = GKO_FMHA_POLY_PAIRS;
 
 struct Params {
   int hq, hkv, group;  // group = hq / hkv
@@ -384,7 +378,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Row maximum. The plain path keeps raw scores (scale > 0 is folded into the
       // exponent FFMA below); the general path converts to log2-domain logits first.
       float kmul;  // multiplier taking s[] to the log2 domain
-      bool emulate = false;
       float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
       if constexpr (EXTRA) {
 #pragma unroll
@@ -407,7 +400,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < kBN; ++c) s[c] = (c < lim) ? s[c] : -INFINITY;
         }
-        emulate = !need_mask;
         kmul = p.scale_log2;
       }
 #pragma unroll
@@ -437,50 +429,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st32(o_tmem + c * 32, o);
         }
       }
-      // P_t = 2^(kmul * s - m): one packed FFMA per pair, then MUFU.EX2 — or, in tiles
-      // without masked keys, the FMA-pipe polynomial for one pair in four. P (bf16/f16
+      // P_t = 2^(kmul * s - m): one packed FFMA per pair, then MUFU.EX2. P (bf16/f16
       // pairs) goes into the first kBN/2 columns of the S_t region, 64 keys at a time.
       const float nm = (m_new == -INFINITY) ? 0.f : -m_new;
       const uint64_t k2 = f2pack(kmul, kmul), nm2 = f2pack(nm, nm);
       float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-      auto exp_row = [&](auto poly_tag) {
-        constexpr bool kPoly = decltype(poly_tag)::value;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t pk[32];
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            uint64_t x = fma2(f2pack(s[half * 64 + 2 * c], s[half * 64 + 2 * c + 1]), k2, nm2);
-            if (kPoly && ((kPolyPairs >> (c & 7)) & 1)) {
-              x = exp2_poly_x2(x);
-            } else {
-              float a, b;
-              f2unpack(x, a, b);
-              x = f2pack(fast_exp2(a), fast_exp2(b));
-            }
-            float a, b;
-            f2unpack(x, a, b);
-            if (c & 1) {
-              acc2 += a;
-              acc3 += b;
-            } else {
-              acc0 += a;
-              acc1 += b;
-            }
-            pk[c] = Cvt<T>::pack(a, b);
+        for (int c = 0; c < 32; ++c) {
+          float a, b;
+          f2unpack(fma2(f2pack(s[half * 64 + 2 * c], s[half * 64 + 2 * c + 1]), k2, nm2), a, b);
+          a = fast_exp2(a);
+          b = fast_exp2(b);
+          if (c & 1) {
+            acc2 += a;
+            acc3 += b;
+          } else {
+            acc0 += a;
+            acc1 += b;
           }
-          tmem_st32(s_tmem + half * 32, pk);
-          // hand this half of P to the MMA warp
-          tmem_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar_pfull + 16 * t + 8 * half);
+          pk[c] = Cvt<T>::pack(a, b);
         }
-      };
-      if (kPolyPairs != 0 && emulate)
-        exp_row(std::true_type{});
-      else
-        exp_row(std::false_type{});
+        tmem_st32(s_tmem + half * 32, pk);
+        // hand this half of P to the MMA warp
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_pfull + 16 * t + 8 * half);
+      }
       const float rsum = (acc0 + acc1) + (acc2 + acc3);
       l_run = l_run * alpha + rsum;
       m_run = m_new;

@@ -571,43 +571,6 @@ __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
   return d;
 }
 
-// 2^x for a pair on the FMA pipe (relieves the MUFU unit in the softmax).
-// Range reduction x = j + f with j = round(x) via the 1.5 * 2^23 addition trick,
-// f in [-0.5, 0.5]; 2^f by a degree-3 polynomial fitted here for minimax relative
-// error on [-0.5, 0.5] (max rel. error 7.5e-5 evaluated in fp32); 2^j is added
-// into the exponent field. Inputs are clamped to >= -125 (results below 2^-125
-// are irrelevant next to the row maximum, which contributes >= 2^-8).
-__device__ __forceinline__ float exp2_poly(float x) {
-  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
-  x = fmaxf(x, -125.f);
-  const float y = x + kRound;
-  const float j = y - kRound;
-  const float f = x - j;
-  float q = fmaf(f, 0.05517166853f, 0.24261112511f);
-  q = fmaf(q, f, 0.69326096773f);
-  q = fmaf(q, f, 0.99992805719f);
-  return __int_as_float(__float_as_int(q) + (__float_as_int(y) << 23));
-}
-
-// The same on a packed pair (f32x2 arithmetic: half the FMA-pipe issue slots).
-__device__ __forceinline__ uint64_t exp2_poly_x2(uint64_t x) {
-  constexpr float kRound = 12582912.0f;
-  float a, b;
-  f2unpack(x, a, b);
-  x = f2pack(fmaxf(a, -125.f), fmaxf(b, -125.f));
-  const uint64_t y = add2(x, f2pack(kRound, kRound));
-  const uint64_t j = add2(y, f2pack(-kRound, -kRound));
-  const uint64_t f = add2(x, j ^ 0x8000000080000000ull);  // x - j
-  uint64_t q = fma2(f, f2pack(0.05517166853f, 0.05517166853f), f2pack(0.24261112511f, 0.24261112511f));
-  q = fma2(q, f, f2pack(0.69326096773f, 0.69326096773f));
-  q = fma2(q, f, f2pack(0.99992805719f, 0.99992805719f));
-  float ql, qh, yl, yh;
-  f2unpack(q, ql, qh);
-  f2unpack(y, yl, yh);
-  return f2pack(__int_as_float(__float_as_int(ql) + (__float_as_int(yl) << 23)),
-                __int_as_float(__float_as_int(qh) + (__float_as_int(yh) << 23)));
-}
-
 // Warpgroup register re-allocation (all 128 threads of the warpgroup execute it).
 template <uint32_t N>
 __device__ __forceinline__ void setmaxnreg_inc() {
