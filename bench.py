@@ -391,7 +391,7 @@ class FmhaBackward(SwigluMLP):
 class SwigluTrain(SwigluMLP):
     """Training step of the fused gate/up SwiGLU (Llama-3-8B MLP shape): forward through
     gko::gemm_swiglu_aux (the kernel also writes the gate/up pre-activations) and backward
-    from them (swiglu_bwd kernel, dX on the tensor-core GEMM, dW on cuBLAS) — no recomputed
+    from them (swiglu_bwd kernel, dX and dW on the tensor-core GEMM) — no recomputed
     forward GEMM. FLOP = 3 x the forward's 2 M D 2H."""
     name = "swiglu_train"
     dominant = "swiglu_gateup"
@@ -409,7 +409,7 @@ class SwigluTrain(SwigluMLP):
         g = torch.Generator(device=dev).manual_seed(1500 + rank)
         self.dy = torch.randn(self.T, self.H, device=dev, generator=g).to(torch.bfloat16)
         self.flop_step = 3.0 * self.flop_gateup
-        self.launches_per_step = 3  # gate/up + aux, swiglu_bwd, dX GEMM (dW runs on cuBLAS)
+        self.launches_per_step = 4  # gate/up + aux, swiglu_bwd, dX GEMM, dW GEMM
         self.config = dict(self.config, workload="swiglu training step, llama3-8b shape: X[8192,4096] bf16, "
                            "W_gate/W_up packed [28672,4096]; step = fused gate/up forward saving gate/up + "
                            "backward (dX, dW) without recomputing the forward GEMM")

@@ -20,10 +20,10 @@ int bias_kind_of(const void* bias, int bias_dtype) {
   }
 }
 
-template <typename T, int EPI, bool B_MN>
+template <typename T, int EPI, bool B_MN, bool A_MN = false>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
               const GemmParams& p, cudaStream_t stream) {
-  auto kern = gemm::gemm_kernel<T, EPI, B_MN>;
+  auto kern = gemm::gemm_kernel<T, EPI, B_MN, A_MN>;
   static bool configured[64] = {false};  // per instantiation and device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -78,7 +78,10 @@ int dispatch_pair(int epi, bool b_mn, const CUtensorMap& ta, const CUtensorMap& 
 
 template <typename T>
 int dispatch_tc(int epi, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                const CUtensorMap& td, const GemmParams& p, cudaStream_t s) {
+                const CUtensorMap& td, const GemmParams& p, cudaStream_t s, bool a_mn = false) {
+  if (a_mn)  // MN-major A: plain epilogue only (checked by the caller)
+    return b_mn ? launch_tc<T, kEpiNone, true, true>(ta, tb, td, p, s)
+                : launch_tc<T, kEpiNone, false, true>(ta, tb, td, p, s);
   if (!b_mn) {
     switch (epi) {
       case kEpiAllReduce: return launch_tc<T, kEpiAllReduce, false>(ta, tb, td, p, s);
@@ -104,7 +107,9 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
            const void* bias, int bias_kind, void* d, int64_t ldd, unsigned* status,
            cudaStream_t stream, void* red_mc = nullptr, void* const* red_peers = nullptr,
            int red_world = 0, void* aux = nullptr, int64_t aux_ld = 0, const void* resid = nullptr,
-           int64_t resid_ld = 0, const float* row_scale = nullptr) {
+           int64_t resid_ld = 0, const float* row_scale = nullptr, bool a_mn = false) {
+  if (a_mn && (epi != kEpiNone || aux || resid || row_scale || red_world))
+    return fail(GKO_ERR_UNSUPPORTED, "a transposed (MN-major) mat1 is supported with the plain epilogue only");
   if (resid && (!host::aligned16(resid) || resid_ld % 8))
     return fail(GKO_ERR_UNSUPPORTED, "the residual needs a 16-byte aligned base and a row stride that is a "
                 "multiple of 8");
@@ -117,7 +122,8 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
                 "tensor-core GEMM needs row strides that are multiples of 8 elements "
                 "(lda=%lld ldb=%lld ldd=%lld)",
                 (long long)lda, (long long)ldb, (long long)ldd);
-  if (K % 8 || N_out % 8)
+  // K is a row count (no alignment rule) only when both operands are MN-major
+  if ((K % 8 && !(a_mn && b_mn)) || N_out % 8)
     return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs K %% 8 == 0 and N %% 8 == 0 "
                 "(K=%lld N=%lld)", (long long)K, (long long)N_out);
   if (b_mn && epi == kEpiSwiglu && up_offset % 8)
@@ -126,10 +132,16 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
     return fail(GKO_ERR_UNSUPPORTED, "GEMM dimensions must be < 2^31");
   const int esz = 2;
   CUtensorMap ta, tb, td;
-  {
+  if (!a_mn) {
     uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
     uint64_t str[1] = {(uint64_t)(lda * esz)};
     uint32_t box[2] = {64, 128};
+    if (!host::encode_tmap(&ta, dtype, 2, a, dims, str, box)) return GKO_ERR_INVALID;
+  } else {
+    // A stored [K, M] row-major (row stride lda): 64 M-columns x 64 K-rows per box
+    uint64_t dims[2] = {(uint64_t)M, (uint64_t)K};
+    uint64_t str[1] = {(uint64_t)(lda * esz)};
+    uint32_t box[2] = {64, 64};
     if (!host::encode_tmap(&ta, dtype, 2, a, dims, str, box)) return GKO_ERR_INVALID;
   }
   if (!b_mn) {
@@ -160,7 +172,7 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
 #ifndef GKO_GEMM_PAIR_MIN_M
 #define GKO_GEMM_PAIR_MIN_M 0x7fffffff
 #endif
-  const bool pair = M >= GKO_GEMM_PAIR_MIN_M && epi != kEpiAllReduce && !aux && !resid && !row_scale;
+  const bool pair = M >= GKO_GEMM_PAIR_MIN_M && epi != kEpiAllReduce && !aux && !resid && !row_scale && !a_mn;
   const int block_m = pair ? 2 * gemm::kBM : gemm::kBM;
   p.m_blocks = (int)((M + block_m - 1) / block_m);
   const int bn = gemm::block_n_out(epi);
@@ -211,8 +223,8 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
     if (dtype == GKO_BF16) return dispatch_pair<__nv_bfloat16>(epi, b_mn, ta, tb, td, p, stream);
     return dispatch_pair<__half>(epi, b_mn, ta, tb, td, p, stream);
   }
-  if (dtype == GKO_BF16) return dispatch_tc<__nv_bfloat16>(epi, b_mn, ta, tb, td, p, stream);
-  return dispatch_tc<__half>(epi, b_mn, ta, tb, td, p, stream);
+  if (dtype == GKO_BF16) return dispatch_tc<__nv_bfloat16>(epi, b_mn, ta, tb, td, p, stream, a_mn);
+  return dispatch_tc<__half>(epi, b_mn, ta, tb, td, p, stream, a_mn);
 }
 
 int run_f32(int epi, int64_t M, int64_t N_out, int64_t K, int64_t up_offset, const float* a,
@@ -270,8 +282,22 @@ extern "C" int gko_addmm_act(int dtype, int act, int64_t m, int64_t n, int64_t k
                    static_cast<const float*>(b), b_sk, b_sn, bias, bk, static_cast<float*>(d),
                    ldd, status, s);
   if (k == 0) return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs k > 0");
+  if (a_sk != 1 && a_sm == 1 && m > 1) {
+    // mat1 = X^T view of a row-major X [k, m] (the weight-gradient GEMM dW = dZ^T X): MN-major A
+    if (epi != kEpiNone)
+      return fail(GKO_ERR_UNSUPPORTED, "a transposed mat1 is supported without an activation only");
+    if (b_sk == 1)
+      return run_tc(dtype, epi, m, n, k, n, 0, a, a_sk, b, b_sn, false, bias, bk, d, ldd, status, s, nullptr,
+                    nullptr, 0, nullptr, 0, nullptr, 0, nullptr, true);
+    if (b_sn == 1)
+      return run_tc(dtype, epi, m, n, k, n, 0, a, a_sk, b, b_sk, true, bias, bk, d, ldd, status, s, nullptr,
+                    nullptr, 0, nullptr, 0, nullptr, 0, nullptr, true);
+    return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs mat2 with unit stride in one dimension");
+  }
   if (a_sk != 1)
-    return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs a row-major mat1 (stride(-1) == 1)");
+    return fail(GKO_ERR_UNSUPPORTED,
+                "tensor-core GEMM needs mat1 with unit stride in one dimension (row-major, or a transposed "
+                "view without an activation)");
   if (b_sk == 1) {
     // mat2 = W^T view of a row-major weight W [n, k]: K-major B.
     return run_tc(dtype, epi, m, n, k, n, 0, a, a_sm, b, b_sn, false, bias, bk, d, ldd, status, s);

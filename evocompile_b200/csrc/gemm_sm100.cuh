@@ -271,13 +271,16 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
   }
 }
 
-template <typename T, int EPI, bool B_MN>
+// A_MN: A stored MN-major ([K, M] row-major, e.g. the transposed view of an activation
+// gradient dZ [tokens, N] when the GEMM computes dW = dZ^T X over the token axis): each stage
+// holds two 64-row M chunks of 64 K-rows, like the MN-major B tile.
+template <typename T, int EPI, bool B_MN, bool A_MN = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                 const __grid_constant__ CUtensorMap tm_d, const GemmParams p) {
   constexpr int kBNOut = block_n_out(EPI);
   constexpr uint32_t kIdesc =
-      make_idesc_f16(std::is_same<T, __nv_bfloat16>::value, kBM, kMmaN, false, B_MN);
+      make_idesc_f16(std::is_same<T, __nv_bfloat16>::value, kBM, kMmaN, A_MN, B_MN);
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
@@ -348,7 +351,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a_dst = sA + stage * kABytes;
           const uint32_t b_dst = sB + stage * kBBytes;
           const int k0 = kb * kBK;
-          tma_load_2d_hint(a_dst, &tm_a, full, k0, mb * kBM, pol_a);
+          if constexpr (A_MN) {
+            // A is [K, M] MN-major: two 64-column boxes, 64 K-rows each.
+            tma_load_2d_hint(a_dst, &tm_a, full, mb * kBM, k0, pol_a);
+            tma_load_2d_hint(a_dst + kABytes / 2, &tm_a, full, mb * kBM + 64, k0, pol_a);
+          } else {
+            tma_load_2d_hint(a_dst, &tm_a, full, k0, mb * kBM, pol_a);
+          }
           if constexpr (!B_MN) {
             // B is [N, K] K-major: two 128-row boxes.
             if constexpr (EPI == kEpiSwiglu) {
@@ -387,9 +396,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Descriptors are built once: a stage or a K step only adds a constant to the 14-bit
       // start-address field (shared-memory addresses stay below 256 KB, so it never carries);
       // building them per MMA costs the issuing thread more than an MMA's execution time.
-      const uint64_t d_a0 = make_sdesc_sw128(sA, 16, 1024);
+      const uint64_t d_a0 = A_MN ? make_sdesc_sw128(sA, kABytes / 2, 1024) : make_sdesc_sw128(sA, 16, 1024);
       const uint64_t d_b0 = B_MN ? make_sdesc_sw128(sB, kBBytes / 4, 1024) : make_sdesc_sw128(sB, 16, 1024);
-      constexpr uint32_t kKStepB = B_MN ? (16 * 128) >> 4 : 32 >> 4;  // per K16 step, 16-byte units
+      constexpr uint32_t kKStepA = A_MN ? (16 * 128) >> 4 : 32 >> 4;  // per K16 step, 16-byte units
+      constexpr uint32_t kKStepB = B_MN ? (16 * 128) >> 4 : 32 >> 4;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
@@ -412,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t acc0 = kb != 0 ? 1u : 0u;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_f16_ss(d_tmem, a_st + kk * (32 >> 4), b_st + kk * kKStepB, kIdesc, kk > 0 ? 1u : acc0);
+            mma_f16_ss(d_tmem, a_st + kk * kKStepA, b_st + kk * kKStepB, kIdesc, kk > 0 ? 1u : acc0);
           mma_commit(bar_empty + 8 * stage);
           if (++stage == kStages) {
             stage = 0;

@@ -28,6 +28,7 @@ from typing import Tuple
 import torch
 
 from .. import _lib, ops
+from . import gemm_ops
 
 aten = torch.ops.aten
 
@@ -43,9 +44,20 @@ def _addmm_gelu_forward(bias, mat1, mat2):
 
 
 def _pre_activation(bias, mat1, mat2):
-    if mat1.dim() == 2 and mat2.dim() == 2:
-        return torch.addmm(bias, mat1, mat2)
-    return torch.matmul(mat1, mat2) + bias
+    """z = mat1 @ mat2 + bias, recomputed on the library GEMM (the reference recomputes it with
+    addmm / matmul, eval/kernels/addmm_gelu.py:175-185)."""
+    z = torch.ops.gko.gemm(mat1.reshape(-1, mat1.shape[-1]), mat2) + bias
+    return z.reshape(*mat1.shape[:-1], mat2.shape[1])
+
+
+def _weight_grad(mat1, g2):
+    """dW = mat1^T @ dZ over all token rows, on the library GEMM with mat1^T read in place."""
+    return torch.ops.gko.gemm(mat1.reshape(-1, mat1.shape[-1]).t(), g2)
+
+
+def _input_grad(g2, mat2, shape):
+    """dX = dZ @ mat2^T (mat2^T is the row-major weight of a Linear) on the library GEMM."""
+    return torch.ops.gko.gemm(g2, mat2.t()).reshape(shape)
 
 
 def _setup_context(ctx, inputs, output):
@@ -60,8 +72,8 @@ def _backward(ctx, grad_output):
     needs = getattr(ctx, "needs_input_grad", None) or (True, True, True)
     g2 = gz.reshape(-1, gz.shape[-1])
     g_bias = g2.sum(0).reshape(bias.shape) if needs[0] else None
-    g_mat1 = g2.mm(mat2.t()).reshape(mat1.shape) if needs[1] else None
-    g_mat2 = mat1.reshape(-1, mat1.shape[-1]).t().mm(g2) if needs[2] else None
+    g_mat1 = _input_grad(g2, mat2, mat1.shape) if needs[1] else None
+    g_mat2 = _weight_grad(mat1, g2) if needs[2] else None
     return g_bias, g_mat1, g_mat2
 
 
@@ -78,9 +90,8 @@ def _backward_aux(ctx, grad_output, grad_z):
     needs = getattr(ctx, "needs_input_grad", None) or (True, True, True)
     g2 = gz.reshape(-1, gz.shape[-1])
     g_bias = g2.sum(0).reshape(bias.shape) if needs[0] else None
-    # dX = dZ @ mat2^T on the tensor-core GEMM (mat2^T is the row-major weight for a Linear)
-    g_mat1 = ops.addmm_act(None, g2, mat2.t(), _lib.ACT_NONE).reshape(mat1.shape) if needs[1] else None
-    g_mat2 = mat1.reshape(-1, mat1.shape[-1]).t().mm(g2) if needs[2] else None
+    g_mat1 = _input_grad(g2, mat2, mat1.shape) if needs[1] else None
+    g_mat2 = _weight_grad(mat1, g2) if needs[2] else None
     return g_bias, g_mat1, g_mat2
 
 
@@ -92,6 +103,7 @@ def addmm_gelu_train(bias, mat1, mat2):
 
 def _ensure_op():
     global _OP_READY, _AUTOGRADED
+    gemm_ops.ensure()
     if not _OP_READY:
         if not (hasattr(torch.ops, "gko") and hasattr(torch.ops.gko, "addmm_gelu")):
 

@@ -20,9 +20,9 @@ from __future__ import annotations
 from typing import Tuple
 
 import torch
-import torch.nn.functional as F
 
 from .. import ops
+from . import gemm_ops
 
 _OP_READY = False
 _AUTOGRADED = False
@@ -40,17 +40,19 @@ def _setup_context(ctx, inputs, output):
 
 
 def _backward(ctx, grad_out):
+    """The reference's backward (eval/kernels/gemm_swiglu.py:177-200): recompute gate/up, then
+    dX and dW; every GEMM on the library's tensor-core kernel."""
     x, weight = ctx.saved_tensors
-    gate, up = F.linear(x, weight).chunk(2, dim=-1)
+    x2 = x.reshape(-1, x.shape[-1])
+    gate, up = torch.ops.gko.gemm(x2, weight.t()).chunk(2, dim=-1)
+    g = grad_out.reshape(-1, grad_out.shape[-1])
     sig = torch.sigmoid(gate)
-    d_up = grad_out * gate * sig
-    d_gate = grad_out * up * (sig * (1 + gate * (1 - sig)))
+    d_up = g * gate * sig
+    d_gate = g * up * (sig * (1 + gate * (1 - sig)))
     d_gu = torch.cat([d_gate, d_up], dim=-1)
     needs = getattr(ctx, "needs_input_grad", None) or (True, True)
-    gx = F.linear(d_gu, weight.t()).reshape(x.shape) if needs[0] else None
-    gw = None
-    if needs[1]:
-        gw = d_gu.reshape(-1, d_gu.shape[-1]).t().mm(x.reshape(-1, x.shape[-1]))
+    gx = torch.ops.gko.gemm(d_gu, weight).reshape(x.shape) if needs[0] else None
+    gw = torch.ops.gko.gemm(d_gu.t(), x2) if needs[1] else None
     return gx, gw
 
 
@@ -60,17 +62,16 @@ def _setup_aux(ctx, inputs, output):
 
 
 def _backward_aux(ctx, grad_out, grad_gu):
-    from .. import _lib
-
     x, weight, gate_up = ctx.saved_tensors
-    d_gu = ops.swiglu_bwd(grad_out.contiguous(), gate_up)
+    d_gu = torch.ops.gko.swiglu_bwd(grad_out, gate_up)
     if grad_gu is not None:
         d_gu = d_gu + grad_gu
     needs = getattr(ctx, "needs_input_grad", None) or (True, True)
     d2 = d_gu.reshape(-1, d_gu.shape[-1])
     # dX = d_gate_up @ [Wg; Wu] on the tensor-core GEMM (the weight read as an MN-major operand)
-    gx = ops.addmm_act(None, d2, weight, _lib.ACT_NONE).reshape(x.shape) if needs[0] else None
-    gw = d2.t().mm(x.reshape(-1, x.shape[-1])) if needs[1] else None
+    gx = torch.ops.gko.gemm(d2, weight).reshape(x.shape) if needs[0] else None
+    # dW = d_gate_up^T @ X over the tokens: d_gate_up^T is read in place as an MN-major operand
+    gw = torch.ops.gko.gemm(d2.t(), x.reshape(-1, x.shape[-1])) if needs[1] else None
     return gx, gw
 
 
@@ -82,6 +83,7 @@ def apply_train(x, weight):
 
 def _ensure_op():
     global _OP_READY, _AUTOGRADED
+    gemm_ops.ensure()
     if not _OP_READY:
         if not (hasattr(torch.ops, "gko") and hasattr(torch.ops.gko, "gemm_swiglu")):
 

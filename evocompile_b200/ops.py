@@ -80,7 +80,11 @@ def addmm_act(bias, mat1, mat2, act: int = _lib.ACT_GELU, save_pre: bool = False
     lead = mat1.shape[:-1]
     a = mat1.reshape(-1, K) if mat1.dim() != 2 else mat1
     M = a.shape[0]
-    if dt != _lib.F32 and a.stride(-1) != 1 and M > 1:
+    # a transposed mat1 (the weight-gradient GEMM dZ^T X) is read in place as an MN-major operand
+    # when no activation or pre-activation output is asked for; other strides are made row-major
+    a_mn = (dt != _lib.F32 and act == _lib.ACT_NONE and not save_pre and M > 1
+            and a.stride(0) == 1 and (K == 1 or a.stride(1) % 8 == 0))
+    if dt != _lib.F32 and a.stride(-1) != 1 and M > 1 and not a_mn:
         a = a.contiguous()
     b = mat2
     if dt != _lib.F32 and not (b.stride(0) == 1 or b.stride(1) == 1):
@@ -104,6 +108,9 @@ def addmm_act(bias, mat1, mat2, act: int = _lib.ACT_GELU, save_pre: bool = False
     if M and N:
         with torch.cuda.device(dev):
             a_sm = a.stride(0) if M > 1 else max(K, 8)
+            a_sk = a.stride(1)
+            if a_mn and K == 1:
+                a_sk = (M + 7) // 8 * 8  # a single row of the [K, M] storage: its stride is never used
             if save_pre:
                 rc = _lib.load().gko_addmm_act_aux(
                     dt, act, M, N, K, _ptr(a), a_sm, a.stride(1), _ptr(b), b.stride(0), b.stride(1),
@@ -112,7 +119,7 @@ def addmm_act(bias, mat1, mat2, act: int = _lib.ACT_GELU, save_pre: bool = False
                 )
             else:
                 rc = _lib.load().gko_addmm_act(
-                    dt, act, M, N, K, _ptr(a), a_sm, a.stride(1), _ptr(b), b.stride(0), b.stride(1),
+                    dt, act, M, N, K, _ptr(a), a_sm, a_sk, _ptr(b), b.stride(0), b.stride(1),
                     _ptr(bias_t), bias_dt, _ptr(out), out.stride(0), _status_ptr(dev), _stream(dev),
                 )
         _lib.check(rc, "gko_addmm_act_aux" if save_pre else "gko_addmm_act")

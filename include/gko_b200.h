@@ -73,7 +73,10 @@ int gko_version(void);
  * bias_dtype. D is [m, n] with row stride ldd, same dtype as A.
  * f16/bf16 run on tcgen05 tensor cores (f32 accumulate) and need
  * a_sk == 1 and (b_sk == 1 or b_sn == 1), 16-byte aligned bases and row
- * strides that are multiples of 8 elements. f32 runs exact fp32 FMA on any strides.
+ * strides that are multiples of 8 elements. With act == GKO_ACT_NONE, A may
+ * also be a transposed view (a_sm == 1, a_sk a multiple of 8): the weight
+ * gradient dW = dZ^T X of a Linear, read in place as an MN-major operand.
+ * f32 runs exact fp32 FMA on any strides.
  */
 int gko_addmm_act(int dtype, int act, int64_t m, int64_t n, int64_t k, const void* a, int64_t a_sm,
                   int64_t a_sk, const void* b, int64_t b_sk, int64_t b_sn, const void* bias,

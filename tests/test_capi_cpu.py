@@ -68,9 +68,12 @@ def test_tensor_core_layout_constraints(lib):
     # K % 8 != 0 -> unsupported (stride rule of the TMA descriptors)
     rc = lib.gko_addmm_act(_lib.BF16, 1, 16, 16, 12, fake, 12, 1, fake, 1, 12, _null(), 0, fake, 16, _null(), _null())
     assert rc == _lib.ERR_UNSUPPORTED and "multiples of 8" in _lib.last_error()
-    # mat1 not row-major
+    # transposed mat1 with an activation: the MN-major A path has the plain epilogue only
     rc = lib.gko_addmm_act(_lib.BF16, 1, 16, 16, 16, fake, 1, 16, fake, 1, 16, _null(), 0, fake, 16, _null(), _null())
-    assert rc == _lib.ERR_UNSUPPORTED and "row-major" in _lib.last_error()
+    assert rc == _lib.ERR_UNSUPPORTED and "without an activation" in _lib.last_error()
+    # mat1 with no unit stride at all
+    rc = lib.gko_addmm_act(_lib.BF16, 0, 16, 16, 16, fake, 32, 2, fake, 1, 16, _null(), 0, fake, 16, _null(), _null())
+    assert rc == _lib.ERR_UNSUPPORTED and "unit stride in one dimension" in _lib.last_error()
 
 
 def _i64x4(*v):

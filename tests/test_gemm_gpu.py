@@ -192,3 +192,47 @@ def test_rejects_unsupported():
     w = torch.randn(32, 12, device=dev).to(torch.bfloat16)
     with pytest.raises(RuntimeError, match="multiples of 8"):
         ops.addmm_act(None, x, w.t())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (264, 200, 1000), (8, 8, 16), (1000, 520, 77 * 8), (4096, 1024, 512),
+                                   (528, 256, 300), (64, 72, 1)])
+@pytest.mark.parametrize("b_layout", ["wt_view", "kn_contig"])
+def test_weight_grad_transposed_mat1(dtype, m, n, k, b_layout):
+    """dW = dZ^T X: mat1 is the transposed view of a row-major [k, m] tensor, read in place as
+    an MN-major operand (no copy); ragged m, n and k."""
+    if b_layout == "wt_view" and k % 8:
+        pytest.skip("a K-major mat2 needs k % 8 == 0 (its rows are k elements)")
+    g = _gen(m + n + k + (b_layout == "wt_view"))
+    a_store = _randn(g, k, m, dtype=dtype)           # e.g. dZ [tokens, features]
+    a = a_store.cuda().t()                            # [m, k], strides (1, m)
+    if b_layout == "kn_contig":
+        b_host = _randn(g, k, n, dtype=dtype)         # e.g. X [tokens, in]
+        b = b_host.cuda()
+    else:
+        b_host = _randn(g, n, k, dtype=dtype).t()
+        b = b_host.t().contiguous().cuda().t()
+    out = ops.addmm_act(None, a, b, _lib.ACT_NONE)
+    torch.cuda.synchronize()
+    _status_clean()
+    ref = a_store.float().t() @ b_host.float()
+    assert out.shape == (m, n)
+    assert oracle.rel_err(out, ref) <= BF16_TOL
+
+
+def test_weight_grad_with_activation_is_refused():
+    """The transposed-mat1 path has the plain epilogue only; with GELU the op copies mat1 to
+    row-major first (same result), and the C ABI refuses the transposed form directly."""
+    import ctypes
+
+    a = torch.randn(64, 128, dtype=torch.bfloat16, device="cuda").t()
+    b = torch.randn(64, 64, dtype=torch.bfloat16, device="cuda")
+    ref = torch.nn.functional.gelu(a.float() @ b.float())
+    assert oracle.rel_err(ops.addmm_act(None, a, b, _lib.ACT_GELU), ref.cpu()) <= BF16_TOL
+    out = torch.empty(128, 64, dtype=torch.bfloat16, device="cuda")
+    dev = torch.device("cuda", 0)
+    rc = _lib.load().gko_addmm_act(
+        _lib.BF16, _lib.ACT_GELU, 128, 64, 64, ctypes.c_void_p(a.data_ptr()), 1, 128, ctypes.c_void_p(b.data_ptr()),
+        64, 1, ctypes.c_void_p(0), 0, ctypes.c_void_p(out.data_ptr()), 64,
+        ctypes.c_void_p(_lib.status_word(dev).data_ptr()), ctypes.c_void_p(_lib.stream_ptr(dev)))
+    assert rc == _lib.ERR_UNSUPPORTED and "transposed" in _lib.last_error()
