@@ -571,7 +571,13 @@ class TPBlockWorkload(SwigluMLP):
         self.flop_step = self.cfg.flops(T, self.S)
         ff_l = self.cfg.d_ff // world
         self.flop_gateup = 2.0 * T * self.cfg.d_model * 2 * ff_l
-        self.launches_per_step = 8  # rms stats, qkv gemm, rope, fmha, o gemm, rms stats, gate/up, down
+        if self.block.comm == "pipe" and world > 1:
+            # the step's events bracket the pipelined post-attention part: o-projection, gate/up
+            # and down GEMMs with their all-reduces
+            self.dominant = "post_attention_pipelined"
+            self.flop_gateup += 2.0 * T * (self.cfg.n_heads // world) * hd * self.cfg.d_model \
+                + 2.0 * T * ff_l * self.cfg.d_model
+        self.launches_per_step = 7  # rms stats, qkv gemm (+ RoPE), fmha, o gemm, rms stats, gate/up, down
         self.config = {
             "workload": "llama3-70b block prefill bf16: d_model 8192, 64 q / 8 kv heads, D 128, d_ff 28672, "
                         "B=4 S=4096; RMSNorm -> QKV -> RoPE(5e5) -> causal GQA FMHA -> o-proj -> residual -> "
@@ -579,8 +585,11 @@ class TPBlockWorkload(SwigluMLP):
             "inputs": "synthetic: weights N(0,0.02) at Llama-3-70B block shapes, x ~ N(0,1)",
             "global_batch": self.B, "seq_len": self.S, "tokens": T,
             "parallelism": f"tp{world} (column-parallel QKV / gate-up, row-parallel o / down; row-parallel sums: "
-                           + ("none" if world == 1 else "inside the GEMM over NVLink (multicast reduction)"
-                              if self.block.comm == "fused" else "NCCL all-reduce") + ")",
+                           + ("none" if world == 1 else {
+                               "fused": "inside the GEMM over NVLink (multicast reduction)",
+                               "nccl": "NCCL all-reduce after each GEMM",
+                               "pipe": f"NCCL all-reduces of {self.block.chunks} token chunks overlapping the "
+                                       f"next chunks' GEMMs"}[self.block.comm]) + ")",
             "l2": "weights 1.7 GB / tp, activations > L2; no flush",
         }
 
@@ -1034,9 +1043,10 @@ def main():
                     help=f"comma-separated per-configuration records to add (default: {','.join(SUB_WORKLOADS)})")
     ap.add_argument("--small", action="store_true",
                     help="attention workloads at B=4, H=16 (a capture-sized case for ncu --set full)")
-    ap.add_argument("--tp-comm", choices=("auto", "fused", "nccl"), default="auto",
-                    help="tp_block: sum row-parallel outputs inside the GEMM (fused), with NCCL, or "
-                         "fused on two ranks and NCCL on more (auto)")
+    ap.add_argument("--tp-comm", choices=("auto", "fused", "nccl", "pipe"), default="auto",
+                    help="tp_block: sum row-parallel outputs inside the GEMM (fused), with a blocking NCCL "
+                         "all-reduce (nccl), with NCCL all-reduces of token chunks overlapping the next "
+                         "chunks' GEMMs (pipe), or per rank count (auto)")
     args = ap.parse_args()
     global SMALL, TP_COMM
     SMALL = args.small

@@ -10,9 +10,9 @@ d_ff/world gate rows and the matching up rows), the down projection row-parallel
 row-parallel outputs are summed with an NCCL all-reduce. RMSNorm weights are replicated.
 
 Every GEMM is the tcgen05 kernel (the SwiGLU one fused), attention the tcgen05 FMHA reading
-q/k/v in place from the QKV output and writing [tokens, heads, d] for the o-projection,
-RoPE and the RMSNorm statistics (``ops.rms_stats``: 1/rms per token, plus the residual sum) are the
-library's memory-bound kernels; each RMSNorm is applied as a per-row scale in the epilogue of the
+q/k/v in place from the QKV output and writing [tokens, heads, d] for the o-projection.
+RoPE runs in the QKV GEMM's epilogue on the fp32 accumulator (head dim 128); the RMSNorm
+statistics (``ops.rms_stats``: 1/rms per token, plus the residual sum) are a memory-bound kernel; each RMSNorm is applied as a per-row scale in the epilogue of the
 GEMM that follows it, with its weight folded into that GEMM's weight (``ops.linear_rowscale``), so
 the normalised activations never go to HBM; the closing residual
 add runs in the down projection's epilogue (``ops.linear_residual``) on one rank, and with NCCL
@@ -107,13 +107,47 @@ def shard_weights(full: dict, cfg: BlockConfig, rank: int, world: int) -> dict:
     }
 
 
+def post_attention_schedule(chunks: int) -> list:
+    """Issue order of the token-chunk pipeline after attention (every step past attention is
+    per token, so the tokens split into ``chunks`` row ranges that flow independently):
+
+    * ("o", c): o-projection GEMM of chunk c (compute stream);
+    * ("ar_o", c): all-reduce of its output (communication stream, after ("o", c));
+    * ("mlp", c): residual add + RMSNorm statistics, gate/up and down GEMMs of chunk c (compute
+      stream, after ("ar_o", c));
+    * ("ar_d", c): all-reduce of the down output (communication stream, after ("mlp", c)).
+
+    Each stream runs its steps in list order. The o-projection of chunk c+1 is issued before the
+    MLP of chunk c, so the compute stream has work while chunk c's o-projection is being summed,
+    and every all-reduce but the last overlaps a later chunk's GEMMs."""
+    if chunks < 1:
+        raise ValueError("chunks must be >= 1")
+    order = []
+    for c in range(chunks):
+        order += [("o", c), ("ar_o", c)]
+        if c:
+            order += [("mlp", c - 1), ("ar_d", c - 1)]
+    order += [("mlp", chunks - 1), ("ar_d", chunks - 1)]
+    return order
+
+
 class TPBlock:
     """One rank of the tensor-parallel block. ``group`` is a torch.distributed process group
-    (NCCL) or None for a single GPU."""
+    (NCCL) or None for a single GPU.
 
-    def __init__(self, local: dict, cfg: BlockConfig, group=None, comm: str = "auto"):
-        if comm not in ("auto", "fused", "nccl"):
-            raise ValueError(f"comm must be 'auto', 'fused' or 'nccl', got {comm!r}")
+    ``comm``: "fused" sums the row-parallel outputs inside the GEMM over NVLink; "nccl" runs each
+    row-parallel GEMM then a blocking NCCL all-reduce; "pipe" splits the tokens after attention
+    into ``chunks`` and pipelines them (``post_attention_schedule``): each chunk's all-reduces run
+    on a communication stream while later chunks' GEMMs run, with the GEMMs capped at all SMs but
+    ``comm_sms`` so that NCCL's kernels have SMs of their own; "auto" picks per rank count."""
+
+    def __init__(self, local: dict, cfg: BlockConfig, group=None, comm: str = "auto", chunks: int = 4,
+                 comm_sms: int = 16):
+        if comm not in ("auto", "fused", "nccl", "pipe"):
+            raise ValueError(f"comm must be 'auto', 'fused', 'nccl' or 'pipe', got {comm!r}")
+        self.chunks = chunks
+        self.comm_sms = comm_sms
+        self._comm_stream = None
         # RMSNorm runs as a per-row scale in the epilogue of the GEMM that follows it, with the
         # norm weight folded into that GEMM's weight once here: w'[n, j] = w[n, j] * g[j]
         self.w = dict(local)
@@ -155,6 +189,57 @@ class TPBlock:
         y = f(x, weight)
         return y if resid is None else resid.add_(y)
 
+    def _post_attention_pipelined(self, attn2d, x2):
+        """o-projection, residual, RMSNorm, SwiGLU MLP and both all-reduces, token chunk by token
+        chunk (``post_attention_schedule``); returns the block output [T, d]."""
+        from .shard import row_range
+
+        w, cfg = self.w, self.cfg
+        T, d = x2.shape
+        chunks = max(1, min(self.chunks, T))
+        rng = [row_range(T, c, chunks) for c in range(chunks)]
+        cur = torch.cuda.current_stream()
+        if self._comm_stream is None:
+            self._comm_stream = torch.cuda.Stream(x2.device)
+        comm = self._comm_stream
+        rank0 = torch.distributed.get_rank(self.group) == 0
+        y = torch.empty(T, d, device=x2.device, dtype=x2.dtype)
+        o, x1, done_o, done_ar, done_mlp = {}, {}, {}, {}, {}
+        sms = torch.cuda.get_device_properties(x2.device).multi_processor_count
+        prev = ops.set_gemm_ctas(max(1, sms - self.comm_sms))
+        try:
+            for kind, c in post_attention_schedule(chunks):
+                a, b = rng[c]
+                if kind == "o":
+                    o[c] = ops.linear(attn2d[a:b], w["wo"])
+                    done_o[c] = torch.cuda.Event()
+                    done_o[c].record(cur)
+                elif kind == "ar_o":
+                    comm.wait_event(done_o[c])
+                    with torch.cuda.stream(comm):
+                        torch.distributed.all_reduce(o[c], op=torch.distributed.ReduceOp.SUM, group=self.group)
+                        done_ar[c] = torch.cuda.Event()
+                        done_ar[c].record(comm)
+                elif kind == "mlp":
+                    cur.wait_event(done_ar[c])
+                    inv2, x1[c] = ops.rms_stats(o[c], cfg.eps, residual=x2[a:b])
+                    g = ops.linear_rowscale(x1[c], w["w_gate_up_n"], inv2, swiglu=True)
+                    if rank0:  # the residual is summed in once, by rank 0's GEMM epilogue
+                        ops.linear_residual(g, w["w_down"], x1[c], out=y[a:b])
+                    else:
+                        ops.linear(g, w["w_down"], out=y[a:b])
+                    done_mlp[c] = torch.cuda.Event()
+                    done_mlp[c].record(cur)
+                else:  # "ar_d"
+                    comm.wait_event(done_mlp[c])
+                    with torch.cuda.stream(comm):
+                        torch.distributed.all_reduce(y[a:b], op=torch.distributed.ReduceOp.SUM, group=self.group)
+        finally:
+            ops.set_gemm_ctas(prev)
+        cur.wait_stream(comm)
+        y.record_stream(comm)
+        return y
+
     def forward(self, x: torch.Tensor, events=None, mark=None) -> torch.Tensor:
         """x [B, S, d_model] (bf16) -> [B, S, d_model]. ``events`` (start, end) CUDA events, if
         given, bracket the fused gate/up kernel (for per-kernel timing). ``mark(name)``, if given,
@@ -170,17 +255,31 @@ class TPBlock:
         mk("start")
         x2 = x.reshape(T, d)
         inv1 = ops.rms_stats(x2, cfg.eps)                                 # 1/rms per token (fp32)
-        qkv = ops.linear_rowscale(x2, w["wqkv_n"], inv1)                  # rmsnorm(x) Wqkv^T  [T, (hq + 2 hkv) * D]
+        # rmsnorm(x) Wqkv^T [T, (hq + 2 hkv) * D]; q and k heads (adjacent in each row) leave the
+        # GEMM epilogue already rotated by RoPE
+        if hd == 128:
+            qkv = ops.linear_rowscale(x2, w["wqkv_n"], inv1, rope=((hq + hkv) * hd, S, cfg.rope_theta))
+        else:
+            qkv = ops.linear_rowscale(x2, w["wqkv_n"], inv1)
+            ops.rope_(qkv[:, : (hq + hkv) * hd].view(T, hq + hkv, hd), cfg.rope_theta, seq_len=S)
         q = qkv[:, : hq * hd].view(T, hq, hd)
         k = qkv[:, hq * hd: (hq + hkv) * hd].view(T, hkv, hd)
         v = qkv[:, (hq + hkv) * hd:].view(T, hkv, hd)
-        # q and k heads are adjacent in each qkv row: one RoPE launch covers both
-        ops.rope_(qkv[:, : (hq + hkv) * hd].view(T, hq + hkv, hd), cfg.rope_theta, seq_len=S)
         mk("qkv")
         as4 = lambda t: t.view(B, S, t.shape[1], hd).transpose(1, 2)     # noqa: E731  [B, H, S, D] views
         attn = torch.empty(T, hq, hd, device=x.device, dtype=x.dtype)
         ops.fmha_fwd(as4(q), as4(k), as4(v), None, hd ** -0.5, 1, out=as4(attn))
         mk("attention")
+        if self.comm == "pipe" and self.world > 1:
+            # ``events`` bracket the whole pipelined post-attention part here (its GEMMs and
+            # all-reduces interleave, so no single kernel can be bracketed)
+            if events is not None:
+                events[0].record()
+            y = self._post_attention_pipelined(attn.view(T, hq * hd), x2).view(B, S, d)
+            if events is not None:
+                events[1].record()
+            mk("post_attention")
+            return y
         o = self._row_parallel(attn.view(T, hq * hd), w["wo"], 0, mark=mark)  # row-parallel partial -> sum
         mk("o_proj")
         inv2, x1 = ops.rms_stats(o, cfg.eps, residual=x2)               # x1 = x + o, 1/rms(x1)

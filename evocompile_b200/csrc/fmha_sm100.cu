@@ -688,7 +688,8 @@ extern "C" int gko_fmha_varlen_fwd(int dtype, int64_t b, int64_t hq, int64_t hkv
     return fail(GKO_ERR_UNSUPPORTED, "fmha needs token/head strides that are multiples of 8");
   if (!host::aligned16(q) || !host::aligned16(k) || !host::aligned16(v) || !host::aligned16(out))
     return fail(GKO_ERR_UNSUPPORTED, "fmha needs 16-byte aligned q, k, v, out");
-  if (tq >= (1ll << 31) || tk >= (1ll << 31)) return fail(GKO_ERR_UNSUPPORTED, "too many tokens");
+  if (tq >= (1ll << 31) || tk >= (1ll << 31) || b * hq >= (1ll << 31))
+    return fail(GKO_ERR_UNSUPPORTED, "too many tokens or (sequence, head) pairs");
   CUtensorMap mq, mk, mv;
   if (!fmha::make_map(&mq, dtype, q, 1, hq, tq, d, tq * q_st, q_sh, q_st) ||
       !fmha::make_map(&mk, dtype, k, 1, hkv, tk > 0 ? tk : 1, d, tk * k_st, k_sh, k_st) ||

@@ -1,6 +1,7 @@
 // C-ABI entry points for the fused GEMM operators (gko_addmm_act, gko_linear_swiglu).
 #include "gemm_f32.cuh"
 #include "gemm_sm100.cuh"
+#include <atomic>
 #include <cmath>
 
 #include "host_common.h"
@@ -9,6 +10,16 @@ using namespace gko;
 using gko::host::fail;
 
 namespace {
+
+// Upper bound on the CTAs (SMs) a tensor-core GEMM launch occupies; 0 = every SM. Set through
+// gko_set_gemm_ctas so that a collective running on another stream keeps SMs of its own.
+std::atomic<int> g_gemm_ctas{0};
+
+int gemm_grid_limit() {
+  const int sms = host::sm_count();
+  const int lim = g_gemm_ctas.load(std::memory_order_relaxed);
+  return (lim > 0 && lim < sms) ? lim : sms;
+}
 
 int bias_kind_of(const void* bias, int bias_dtype) {
   if (!bias) return kBiasNone;
@@ -33,7 +44,8 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& t
     if (e != cudaSuccess) return host::cuda_check(e, "cudaFuncSetAttribute(gemm)");
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  const int grid = p.num_tiles < host::sm_count() ? p.num_tiles : host::sm_count();
+  const int limit = gemm_grid_limit();
+  const int grid = p.num_tiles < limit ? p.num_tiles : limit;
   kern<<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(ta, tb, td, p);
   return host::cuda_check(cudaGetLastError(), "gemm kernel launch");
 }
@@ -51,7 +63,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
     if (e != cudaSuccess) return host::cuda_check(e, "cudaFuncSetAttribute(gemm pair)");
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  const int pairs = host::sm_count() / 2;
+  const int pairs = gemm_grid_limit() / 2;
   const int clusters = p.num_tiles < pairs ? p.num_tiles : pairs;
   kern<<<2 * clusters, gemm::kThreads, gemm::kPairSmemBytes, stream>>>(ta, tb, td, p);
   return host::cuda_check(cudaGetLastError(), "gemm pair kernel launch");
@@ -107,7 +119,12 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
            const void* bias, int bias_kind, void* d, int64_t ldd, unsigned* status,
            cudaStream_t stream, void* red_mc = nullptr, void* const* red_peers = nullptr,
            int red_world = 0, void* aux = nullptr, int64_t aux_ld = 0, const void* resid = nullptr,
-           int64_t resid_ld = 0, const float* row_scale = nullptr, bool a_mn = false) {
+           int64_t resid_ld = 0, const float* row_scale = nullptr, bool a_mn = false, int rope_cols = 0,
+           int rope_seq = 0, float rope_log2_theta = 0.f) {
+  if (rope_cols > 0 && (epi != kEpiNone || bias || aux || resid || red_world || rope_cols % 128 || rope_seq <= 0 ||
+                        rope_cols > N_out))
+    return fail(GKO_ERR_UNSUPPORTED, "RoPE in the GEMM epilogue needs the plain epilogue (no bias, residual or "
+                "pre-activation output), whole 128-column heads and a positive sequence length");
   if (a_mn && (epi != kEpiNone || aux || resid || row_scale || red_world))
     return fail(GKO_ERR_UNSUPPORTED, "a transposed (MN-major) mat1 is supported with the plain epilogue only");
   if (resid && (!host::aligned16(resid) || resid_ld % 8))
@@ -218,6 +235,9 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
   p.resid = resid;
   p.resid_ld = resid_ld;
   p.row_scale = row_scale;
+  p.rope_cols = rope_cols;
+  p.rope_seq = rope_seq;
+  p.rope_log2_theta = rope_log2_theta;
   if (p.num_tiles == 0) return GKO_OK;
   if (pair) {
     if (dtype == GKO_BF16) return dispatch_pair<__nv_bfloat16>(epi, b_mn, ta, tb, td, p, stream);
@@ -439,4 +459,33 @@ extern "C" int gko_linear_rowscale(int dtype, int swiglu, int64_t m, int64_t n, 
   }
   return run_tc(dtype, kEpiNone, m, n, k, n, 0, x, x_sm, w, w_sn, false, nullptr, kBiasNone, out, ldo, status, s,
                 nullptr, nullptr, 0, nullptr, 0, nullptr, 0, row_scale);
+}
+
+extern "C" int gko_linear_rowscale_rope(int dtype, int64_t m, int64_t n, int64_t k, const void* x, int64_t x_sm,
+                                        int64_t x_sk, const void* w, int64_t w_sn, int64_t w_sk,
+                                        const float* row_scale, void* out, int64_t ldo, int64_t rope_cols,
+                                        int64_t seq_len, float theta, unsigned int* status, void* stream) {
+  if (dtype != GKO_BF16 && dtype != GKO_F16)
+    return fail(GKO_ERR_UNSUPPORTED, "linear_rowscale_rope runs on the bf16 / f16 tensor-core path only");
+  if (m < 0 || n < 0 || k < 0) return fail(GKO_ERR_INVALID, "negative GEMM size");
+  if (rope_cols < 0 || rope_cols > n || rope_cols % 128 || seq_len <= 0 || seq_len >= (1ll << 31))
+    return fail(GKO_ERR_INVALID, "rope_cols must be a multiple of 128 within n, and seq_len positive");
+  if (!(theta > 1.f)) return fail(GKO_ERR_INVALID, "rope theta must be > 1");
+  if (m == 0 || n == 0) return GKO_OK;
+  if (!out || !row_scale || (k && (!x || !w))) return fail(GKO_ERR_INVALID, "null operand pointer");
+  if (k == 0) return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs k > 0");
+  if (x_sk != 1 || w_sk != 1)
+    return fail(GKO_ERR_UNSUPPORTED, "linear_rowscale_rope needs row-major x [m, k] and weight [rows, k]");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return run_tc(dtype, kEpiNone, m, n, k, n, 0, x, x_sm, w, w_sn, false, nullptr, kBiasNone, out, ldo, status, s,
+                nullptr, nullptr, 0, nullptr, 0, nullptr, 0, row_scale, false, (int)rope_cols, (int)seq_len,
+                log2f(theta));
+}
+
+extern "C" int gko_set_gemm_ctas(int ctas) {
+  if (ctas < 0) {
+    fail(GKO_ERR_INVALID, "gemm CTA limit must be >= 0 (0: every SM)");
+    return -1;
+  }
+  return g_gemm_ctas.exchange(ctas);
 }

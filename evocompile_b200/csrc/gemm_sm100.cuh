@@ -65,6 +65,13 @@ struct GemmParams {
   // D = act(s_r * (A*B^T) + bias) + R; SwiGLU: silu(s_r g) * (s_r u). With s = 1/rms(A row)
   // and the RMSNorm weight folded into B, the GEMM computes rmsnorm(A) * B^T.
   const float* row_scale;
+  // Optional rotate-half RoPE (rope_cols > 0, kEpiNone, head dim 128): output columns
+  // [0, rope_cols) are heads of 128 whose pairs (i, i + 64) are rotated by the angle
+  // (row % rope_seq) * theta^(-2i/128) after the row scale, before rounding to T. The QKV
+  // projection of a Llama block writes its q and k heads already rotated.
+  int rope_cols;
+  int rope_seq;
+  float rope_log2_theta;
 };
 
 namespace gemm {
@@ -196,6 +203,29 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
           const int row = row0 + lane, col = col_base + col0;
           store_aux_row<T>(p.aux, p.aux_ld, row, col, p.M, p.N_out, zg);
           store_aux_row<T>(p.aux, p.aux_ld, row, p.N_out + col, p.M, 2 * p.N_out, zu);
+        }
+      } else if (EPI == kEpiNone && p.rope_cols > 0 && col_base + c * 64 < p.rope_cols) {
+        // this chunk is one half of a 128-column head: its partner half is 64 columns away
+        const int hi = cc;  // 0: columns i of the head, 1: columns i + 64
+        uint32_t v[32], w[32];
+        tmem_ld32(t_row + col0, v);
+        tmem_ld32(t_row + col0 + (hi ? -64 : 64), w);
+        tmem_wait_ld();
+        const float pos = (float)((row0 + lane) % p.rope_seq);
+        const int i0 = (col0 & 63);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float o[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int idx = i0 + 2 * i + e;
+            const float inv_freq = exp2f(-p.rope_log2_theta * (2.f * (float)idx / 128.f));
+            float sn, cs;
+            sincosf(pos * inv_freq, &sn, &cs);
+            const float x = __uint_as_float(v[2 * i + e]) * rs, y = __uint_as_float(w[2 * i + e]) * rs;
+            o[e] = hi ? fmaf(x, cs, y * sn) : fmaf(x, cs, -y * sn);
+          }
+          packed[i] = Cvt<T>::pack(o[0], o[1]);
         }
       } else {
         uint32_t v[32];

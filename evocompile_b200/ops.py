@@ -56,7 +56,16 @@ def _check_no_overlap(name, out, **operands):
 
 
 # --------------------------------------------------------------------------- GEMM
-def addmm_act(bias, mat1, mat2, act: int = _lib.ACT_GELU, save_pre: bool = False):
+def set_gemm_ctas(ctas: int) -> int:
+    """Cap the SMs every tensor-core GEMM launched afterwards occupies (0: all); returns the
+    previous cap. Leaves SMs to a collective running on another stream (gko_set_gemm_ctas)."""
+    prev = _lib.load().gko_set_gemm_ctas(int(ctas))
+    if prev < 0:
+        _lib.check(_lib.ERR_INVALID, "gko_set_gemm_ctas")
+    return prev
+
+
+def addmm_act(bias, mat1, mat2, act: int = _lib.ACT_GELU, save_pre: bool = False, out=None):
     """act(mat1 @ mat2 + bias) with mat1 [..., K] and mat2 [K, N].
 
     Follows the contract of gko::addmm_gelu (eval/kernels/addmm_gelu.py:150-161,
@@ -103,7 +112,12 @@ def addmm_act(bias, mat1, mat2, act: int = _lib.ACT_GELU, save_pre: bool = False
         if bias_t.stride(0) != 1:
             bias_t = bias_t.contiguous()
         bias_dt = _lib.dtype_code(bias_t.dtype)
-    out = torch.empty((M, N), device=dev, dtype=mat1.dtype)
+    if out is None:
+        out = torch.empty((M, N), device=dev, dtype=mat1.dtype)
+    elif mat1.dim() != 2 or tuple(out.shape) != (M, N) or out.dtype != mat1.dtype or out.stride(1) != 1:
+        raise RuntimeError("addmm_act: out must be a row-major [m, n] tensor of mat1's dtype (2-D mat1)")
+    else:
+        _check_no_overlap("addmm_act", out, mat1=mat1, mat2=mat2)
     z = torch.empty((M, N), device=dev, dtype=mat1.dtype) if save_pre else None
     if M and N:
         with torch.cuda.device(dev):
@@ -128,9 +142,10 @@ def addmm_act(bias, mat1, mat2, act: int = _lib.ACT_GELU, save_pre: bool = False
     return out.reshape(*lead, N)
 
 
-def linear(x, weight, bias=None):
-    """x @ weight.T (+ bias) on the tensor-core GEMM (the down-projection path)."""
-    return addmm_act(bias, x, weight.t(), _lib.ACT_NONE)
+def linear(x, weight, bias=None, out=None):
+    """x @ weight.T (+ bias) on the tensor-core GEMM (the down-projection path); ``out`` (2-D x
+    only) receives the result in place of a new tensor."""
+    return addmm_act(bias, x, weight.t(), _lib.ACT_NONE, out=out)
 
 
 def linear_swiglu(x, weight, save_pre: bool = False):
@@ -638,10 +653,13 @@ def fold_rmsnorm_weight(weight, norm_weight):
     return (weight.float() * norm_weight.float().view(1, -1)).to(weight.dtype)
 
 
-def linear_rowscale(x, weight, row_scale, swiglu: bool = False):
+def linear_rowscale(x, weight, row_scale, swiglu: bool = False, rope=None):
     """out = row_scale[:, None] * (x @ weight^T) on the tensor-core GEMM (the scale applied to the
     accumulator in the epilogue); with swiglu, weight = [Wg; Wu] (2H, K) and
-    out = silu(s x Wg^T) * (s x Wu^T) (rows, H). x [rows, K] row-major, row_scale fp32 [rows]."""
+    out = silu(s x Wg^T) * (s x Wu^T) (rows, H). x [rows, K] row-major, row_scale fp32 [rows].
+
+    ``rope = (rope_cols, seq_len, theta)`` also rotates output columns [0, rope_cols) (heads of
+    128) with rotate-half RoPE at position row % seq_len, in the epilogue (gko_linear_rowscale_rope)."""
     dev = _lib.require_cuda(x, weight, row_scale)
     if x.dim() != 2 or weight.dim() != 2 or row_scale.dim() != 1:
         raise RuntimeError("linear_rowscale: x [m, k], weight [n, k], row_scale [m]")
@@ -660,6 +678,19 @@ def linear_rowscale(x, weight, row_scale, swiglu: bool = False):
         weight = weight.contiguous()
     row_scale = row_scale.contiguous()
     out = torch.empty(m, n, device=x.device, dtype=x.dtype)
+    if rope is not None:
+        if swiglu:
+            raise RuntimeError("linear_rowscale: RoPE applies to the plain (non-SwiGLU) projection only")
+        rope_cols, seq_len, theta = rope
+        if m and n:
+            with torch.cuda.device(dev):
+                rc = _lib.load().gko_linear_rowscale_rope(
+                    _lib.dtype_code(x.dtype), m, n, k, _ptr(x), x.stride(0), 1, _ptr(weight), weight.stride(0), 1,
+                    _ptr(row_scale), _ptr(out), out.stride(0), int(rope_cols), int(seq_len), float(theta),
+                    _status_ptr(dev), _stream(dev),
+                )
+            _lib.check(rc, "gko_linear_rowscale_rope")
+        return out
     if m and n:
         with torch.cuda.device(dev):
             rc = _lib.load().gko_linear_rowscale(

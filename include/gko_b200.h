@@ -314,6 +314,32 @@ int gko_linear_rowscale(int dtype, int swiglu, int64_t m, int64_t n, int64_t k, 
                         int64_t ldo, unsigned int* status, void* stream);
 
 /*
+ * gko_linear_rowscale (swiglu = 0) whose epilogue also applies rotate-half RoPE to output columns
+ * [0, rope_cols): heads of 128 columns, pair (i, i + 64) of a head at row r rotated by the angle
+ * (r % seq_len) * theta^(-2i/128), computed on the fp32 accumulator before the one rounding to
+ * bf16 / f16. The QKV projection of a Llama block (q heads, then k heads, then v heads) passes
+ * rope_cols = (q heads + k heads) * 128 and writes q and k already rotated.
+ *
+ * No reference counterpart (the block's RoPE; the reference has no transformer block on its kernel
+ * path): it replaces the block's separate in-place gko_rope launch over the q and k heads.
+ */
+int gko_linear_rowscale_rope(int dtype, int64_t m, int64_t n, int64_t k, const void* x, int64_t x_sm,
+                             int64_t x_sk, const void* w, int64_t w_sn, int64_t w_sk, const float* row_scale,
+                             void* out, int64_t ldo, int64_t rope_cols, int64_t seq_len, float theta,
+                             unsigned int* status, void* stream);
+
+/*
+ * Caps the CTAs a tensor-core GEMM launch occupies at `ctas` SMs (0: every SM, the default) for
+ * every GEMM launched after the call, from any host thread. Returns the previous cap, or -1
+ * (with gko_last_error set) when ctas < 0. The persistent
+ * GEMM otherwise holds every SM, so a collective launched on another stream (the tensor-parallel
+ * block's NCCL all-reduce of one token chunk while the next chunk's GEMMs run) would wait for it.
+ *
+ * No reference counterpart (the reference has no tensor parallelism).
+ */
+int gko_set_gemm_ctas(int ctas);
+
+/*
  * y = rmsnorm(x + residual) * weight over rows of `cols` elements (row stride ld),
  * rmsnorm(v) = v / sqrt(mean(v^2) + eps). residual may be NULL; when sum_out is
  * not NULL it receives x + residual (the updated residual stream). bf16/f16,

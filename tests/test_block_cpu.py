@@ -98,3 +98,98 @@ def test_comm_auto_policy(monkeypatch):
 
     with pytest.raises(ValueError):
         TPBlock(local, CFG, comm="ring")
+
+
+def test_post_attention_schedule_orders_each_stream():
+    """Every step appears once; on each stream the steps of a chunk follow its dependencies
+    (o before its all-reduce, that all-reduce before the chunk's MLP, the MLP before the down
+    all-reduce), so the two in-order streams cannot wait on each other in a cycle."""
+    from evocompile_b200.block import post_attention_schedule
+
+    for chunks in (1, 2, 4, 7):
+        order = post_attention_schedule(chunks)
+        assert sorted(order) == sorted((k, c) for c in range(chunks) for k in ("o", "ar_o", "mlp", "ar_d"))
+        pos = {step: i for i, step in enumerate(order)}
+        for c in range(chunks):
+            assert pos[("o", c)] < pos[("ar_o", c)] < pos[("mlp", c)] < pos[("ar_d", c)]
+        compute = [s for s in order if s[0] in ("o", "mlp")]
+        comm = [s for s in order if s[0] in ("ar_o", "ar_d")]
+        # a step waits only on steps of the other stream issued before it in the global order:
+        # simulate both in-order streams to completion
+        done, ic, im = set(), 0, 0
+        deps = {("ar_o", c): ("o", c) for c in range(chunks)}
+        deps.update({("mlp", c): ("ar_o", c) for c in range(chunks)})
+        deps.update({("ar_d", c): ("mlp", c) for c in range(chunks)})
+        while ic < len(compute) or im < len(comm):
+            moved = False
+            if ic < len(compute) and deps.get(compute[ic], None) in (None, *done):
+                done.add(compute[ic]); ic += 1; moved = True
+            if im < len(comm) and deps[comm[im]] in done:
+                done.add(comm[im]); im += 1; moved = True
+            assert moved, f"streams deadlock at {compute[ic:ic + 1]} / {comm[im:im + 1]}"
+    import pytest
+
+    with pytest.raises(ValueError):
+        post_attention_schedule(0)
+
+
+def _chunked_worker(rank, world, port, q):
+    """The pipelined data flow (per-chunk all-reduces of the o-projection and down outputs) on CPU
+    ranks equals the unsharded block."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from evocompile_b200.block import post_attention_schedule
+        from evocompile_b200.shard import row_range
+
+        full = init_weights(CFG, "cpu", torch.float32, seed=0)
+        local = shard_weights(full, CFG, rank, world)
+        x = torch.randn(1, 30, CFG.d_model, generator=torch.Generator().manual_seed(1))
+        B, S, d = x.shape
+        hd, hq, hkv = CFG.head_dim, local["hq_local"], local["hkv_local"]
+        h = oracle.rmsnorm(x, local["attn_norm"], CFG.eps)
+        qkv = F.linear(h, local["wqkv"].float())
+        qh = oracle.rope(qkv[0, :, : hq * hd].reshape(S, hq, hd), CFG.rope_theta)
+        kh = oracle.rope(qkv[0, :, hq * hd: (hq + hkv) * hd].reshape(S, hkv, hd), CFG.rope_theta)
+        vh = qkv[0, :, (hq + hkv) * hd:].reshape(S, hkv, hd)
+        att, _ = oracle.attention(qh.transpose(0, 1)[None], kh.transpose(0, 1)[None], vh.transpose(0, 1)[None],
+                                  None, hd ** -0.5, 1)
+        attn2d = att[0].transpose(0, 1).reshape(S, hq * hd)
+        x2 = x[0]
+        chunks = 4
+        rng = [row_range(S, c, chunks) for c in range(chunks)]
+        y = torch.empty(S, d)
+        o = {}
+        for kind, c in post_attention_schedule(chunks):
+            a, b = rng[c]
+            if kind == "o":
+                o[c] = F.linear(attn2d[a:b], local["wo"].float())
+            elif kind == "ar_o":
+                dist.all_reduce(o[c])
+            elif kind == "mlp":
+                x1 = x2[a:b] + o[c]
+                h2 = oracle.rmsnorm(x1, local["mlp_norm"], CFG.eps)
+                gu = F.linear(h2, local["w_gate_up"].float())
+                g = F.silu(gu[:, : gu.shape[-1] // 2]) * gu[:, gu.shape[-1] // 2:]
+                y[a:b] = F.linear(g, local["w_down"].float()) + (x1 if rank == 0 else 0)
+            else:
+                dist.all_reduce(y[a:b])
+        if rank == 0:
+            ref = oracle.llama_block(x, full, CFG)[0]
+            q.put(float((y - ref).abs().max() / ref.abs().max()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_pipelined_tp2_matches_unsharded():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 32600 + random.Random().randint(0, 2000)
+    procs = [ctx.Process(target=_chunked_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    err = q.get(timeout=180)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert err < 1e-5

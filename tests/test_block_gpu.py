@@ -236,3 +236,38 @@ def test_block_full_width_full_sequence():
     """Llama-3-70B widths on one full 4096-token sequence: RoPE positions and the causal range
     reach the configuration's whole length (the fp32 oracle runs on the host cores)."""
     assert _block_check(BlockConfig(), 1, 4096) <= TOL
+
+
+@pytest.mark.parametrize("m,k,heads,seq", [(300, 512, (2, 1, 1), 100), (129, 256, (4, 2, 2), 129), (64, 1024, (1, 1, 0), 7)])
+def test_rowscale_rope_epilogue(m, k, heads, seq):
+    """The QKV projection with RMSNorm folded in and RoPE applied in the GEMM epilogue: q and k
+    heads rotated at position row % seq, v heads untouched, against the fp32 oracle."""
+    hq, hk, hv = heads
+    n = (hq + hk + hv) * 128
+    gen = torch.Generator().manual_seed(m + k + n)
+    x = torch.randn(m, k, generator=gen).to(torch.bfloat16)
+    gnorm = (1 + 0.2 * torch.randn(k, generator=gen)).to(torch.bfloat16)
+    w = (torch.randn(n, k, generator=gen) * k ** -0.5).to(torch.bfloat16)
+    dev = torch.device("cuda", 0)
+    xd = x.to(dev)
+    rope_cols = (hq + hk) * 128
+    out = ops.linear_rowscale(xd, ops.fold_rmsnorm_weight(w.to(dev), gnorm.to(dev)), ops.rms_stats(xd, 1e-5),
+                              rope=(rope_cols, seq, 500000.0))
+    torch.cuda.synchronize()
+    assert _lib.read_status(dev) == 0
+    z = oracle.rmsnorm(x, gnorm, 1e-5) @ w.float().t()
+    ref = z.clone()
+    if rope_cols:
+        ref[:, :rope_cols] = oracle.rope(z[:, :rope_cols].view(m, hq + hk, 128), 500000.0,
+                                         torch.arange(m) % seq).reshape(m, rope_cols)
+    assert oracle.rel_err(out, ref) <= TOL
+    if hv:
+        assert oracle.rel_err(out[:, rope_cols:], z[:, rope_cols:]) <= TOL
+
+
+def test_rowscale_rope_rejects_partial_heads():
+    x = torch.zeros(8, 64, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(256, 64, dtype=torch.bfloat16, device="cuda")
+    s = torch.ones(8, dtype=torch.float32, device="cuda")
+    with pytest.raises(RuntimeError, match="multiple of 128"):
+        ops.linear_rowscale(x, w, s, rope=(64, 8, 500000.0))

@@ -236,3 +236,22 @@ def test_weight_grad_with_activation_is_refused():
         64, 1, ctypes.c_void_p(0), 0, ctypes.c_void_p(out.data_ptr()), 64,
         ctypes.c_void_p(_lib.status_word(dev).data_ptr()), ctypes.c_void_p(_lib.stream_ptr(dev)))
     assert rc == _lib.ERR_UNSUPPORTED and "transposed" in _lib.last_error()
+
+
+def test_gemm_cta_cap_keeps_results():
+    """A GEMM confined to a few SMs (gko_set_gemm_ctas) computes the same result; the cap is
+    restored afterwards and a negative cap is refused."""
+    g = _gen(91)
+    x = _randn(g, 1000, 512, dtype=torch.bfloat16).cuda()
+    w = _randn(g, 768, 512, std=512 ** -0.5, dtype=torch.bfloat16).cuda()
+    full = ops.linear(x, w)
+    prev = ops.set_gemm_ctas(7)
+    try:
+        capped = ops.linear(x, w)
+    finally:
+        assert ops.set_gemm_ctas(prev) == 7
+    torch.cuda.synchronize()
+    _status_clean()
+    assert torch.equal(full, capped)
+    with pytest.raises(RuntimeError, match="CTA limit"):
+        ops.set_gemm_ctas(-1)
