@@ -51,6 +51,9 @@ SMALL = False
 # --tp-comm: how the tensor-parallel block sums its row-parallel outputs ("fused": inside the
 # GEMM over NVLink; "nccl": GEMM then NCCL all-reduce; "auto": fused on two ranks, NCCL on more)
 TP_COMM = "auto"
+# --tp-chunks / --tp-comm-sms: token chunks of the pipelined form and the SMs its GEMMs leave free
+TP_CHUNKS = 4
+TP_COMM_SMS = 16
 
 
 # --------------------------------------------------------------------------- helpers
@@ -561,7 +564,8 @@ class TPBlockWorkload(SwigluMLP):
             import torch.distributed as dist
 
             group = dist.group.WORLD
-        self.block = TPBlock(shard_weights(full, self.cfg, rank, world), self.cfg, group, comm=TP_COMM)
+        self.block = TPBlock(shard_weights(full, self.cfg, rank, world), self.cfg, group, comm=TP_COMM,
+                             chunks=TP_CHUNKS, comm_sms=TP_COMM_SMS)
         if world > 1:
             del full
             torch.cuda.empty_cache()
@@ -1047,10 +1051,14 @@ def main():
                     help="tp_block: sum row-parallel outputs inside the GEMM (fused), with a blocking NCCL "
                          "all-reduce (nccl), with NCCL all-reduces of token chunks overlapping the next "
                          "chunks' GEMMs (pipe), or per rank count (auto)")
+    ap.add_argument("--tp-chunks", type=int, default=4, help="tp_block pipe: token chunks")
+    ap.add_argument("--tp-comm-sms", type=int, default=16, help="tp_block pipe: SMs the GEMMs leave to NCCL")
     args = ap.parse_args()
-    global SMALL, TP_COMM
+    global SMALL, TP_COMM, TP_CHUNKS, TP_COMM_SMS
     SMALL = args.small
     TP_COMM = args.tp_comm
+    TP_CHUNKS = args.tp_chunks
+    TP_COMM_SMS = args.tp_comm_sms
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -255,3 +255,25 @@ def test_gemm_cta_cap_keeps_results():
     assert torch.equal(full, capped)
     with pytest.raises(RuntimeError, match="CTA limit"):
         ops.set_gemm_ctas(-1)
+
+
+def test_gelu_epilogue_within_one_bf16_ulp():
+    """The tensor-core epilogue's GELU (erf from Abramowitz & Stegun 7.1.26, |error| <= 1.5e-7) on
+    exactly known pre-activations z (one-hot mat1 rows): every output is within one bf16 ulp of
+    the exact-erf GELU of z rounded to bf16, or, in the negative tail where GELU is tiny and
+    1 + erf cancels (for CUDA's erff too), within an absolute 2e-7 |z|."""
+    z = torch.linspace(-8, 8, 4096).to(torch.bfloat16)
+    m = z.numel()
+    a = torch.zeros(m, 8, dtype=torch.bfloat16)
+    a[:, 0] = z
+    b = torch.zeros(8, 16, dtype=torch.bfloat16)
+    b[0, :] = 1
+    out = ops.addmm_act(None, a.cuda(), b.cuda(), _lib.ACT_GELU)
+    torch.cuda.synchronize()
+    _status_clean()
+    exact = torch.nn.functional.gelu(z.double(), approximate="none")
+    got = out[:, 0].cpu().double()
+    ref = exact.to(torch.bfloat16).double()
+    ulp = torch.maximum(ref.abs(), torch.full_like(ref, 2 ** -126)) * 2 ** -7
+    assert ((got - ref).abs() <= ulp + 2e-7 * z.double().abs() + 1e-30).all()
+    assert torch.equal(out[:, 0], out[:, 15])
