@@ -130,8 +130,9 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
   if (resid && (!host::aligned16(resid) || resid_ld % 8))
     return fail(GKO_ERR_UNSUPPORTED, "the residual needs a 16-byte aligned base and a row stride that is a "
                 "multiple of 8");
-  if (!host::aligned16(a) || !host::aligned16(b) || !host::aligned16(d) || (aux && !host::aligned16(aux)))
-    return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs 16-byte aligned operand bases");
+  if (!host::aligned16(a) || !host::aligned16(b) || !host::aligned16(d) || (aux && !host::aligned16(aux)) ||
+      (bias && !host::aligned16(bias)))
+    return fail(GKO_ERR_UNSUPPORTED, "tensor-core GEMM needs 16-byte aligned operand and bias bases");
   if (aux && aux_ld % 8)
     return fail(GKO_ERR_UNSUPPORTED, "the pre-activation output needs a row stride that is a multiple of 8");
   if (lda % 8 || ldb % 8 || ldd % 8)

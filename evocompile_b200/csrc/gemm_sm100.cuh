@@ -120,23 +120,72 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
 }
 
-// Exact-erf GELU for the bf16 / f16 epilogue, with erf evaluated by Abramowitz & Stegun 7.1.26
-// (Handbook of Mathematical Functions, 1964): erf(z) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5))))
-// e^(-z^2), t = 1 / (1 + p z) for z >= 0, odd extension for z < 0; maximum absolute error
-// 1.5e-7, far below the bf16 rounding of the output (2^-9 relative). Two MUFU operations
-// (reciprocal, exp2) and six FMAs per element: on B200 erff made the GELU epilogue cost 4-8 %
-// of the GEMM's time at K = 4096, against none for ReLU.
-__device__ __forceinline__ float gelu_erf_epilogue(float x) {
-  const float z = fabsf(x) * 0.70710678118654752f;
-  float t;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, z, 1.f)));
-  const float poly =
-      t * fmaf(fmaf(fmaf(fmaf(1.061405429f, t, -1.453152027f), t, 1.421413741f), t, -0.284496736f), t,
-               0.254829592f);
-  float e;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-z * z * 1.4426950408889634f));
-  const float erf_abs = fmaf(-poly, e, 1.f);
-  return 0.5f * x * (1.f + copysignf(erf_abs, x));
+// Exact-erf GELU for the bf16 / f16 epilogue, on a packed pair, with erf evaluated by
+// Abramowitz & Stegun 7.1.28 (Handbook of Mathematical Functions, 1964):
+//   erf(z) = 1 - 1 / (1 + a1 z + a2 z^2 + ... + a6 z^6)^16   for z >= 0 (odd extension below),
+// maximum absolute error 3e-7, far below the bf16 rounding of the output (2^-9 relative). The
+// polynomial and the 16th power run as f32x2 FMAs / multiplies, the reciprocal on the MUFU (one
+// per element; for large z the power overflows to +inf and the reciprocal gives 0). The
+// epilogue's issue slots are shared with the MMA-issuing warp, and on B200 CUDA's erff made the
+// GELU epilogue cost 4-8 % of the GEMM's time at K = 4096 and 15 % at K = 1024.
+__device__ __forceinline__ uint64_t gelu_erf_pair(uint64_t x) {
+  constexpr float kInvSqrt2 = 0.70710678118654752f;
+  float x0, x1;
+  f2unpack(x, x0, x1);
+  const uint64_t z = f2pack(fabsf(x0) * kInvSqrt2, fabsf(x1) * kInvSqrt2);
+  uint64_t q = fma2(z, f2pack(0.0000430638f, 0.0000430638f), f2pack(0.0002765672f, 0.0002765672f));
+  q = fma2(q, z, f2pack(0.0001520143f, 0.0001520143f));
+  q = fma2(q, z, f2pack(0.0092705272f, 0.0092705272f));
+  q = fma2(q, z, f2pack(0.0422820123f, 0.0422820123f));
+  q = fma2(q, z, f2pack(0.0705230784f, 0.0705230784f));
+  q = fma2(q, z, f2pack(1.f, 1.f));
+  q = mul2(q, q);  // ^2
+  q = mul2(q, q);  // ^4
+  q = mul2(q, q);  // ^8
+  q = mul2(q, q);  // ^16
+  float q0, q1, r0, r1;
+  f2unpack(q, q0, q1);
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(q0));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(q1));
+  // 0.5 x (1 + sign(x) (1 - r))
+  const float e0 = copysignf(1.f - r0, x0), e1 = copysignf(1.f - r1, x1);
+  return mul2(f2pack(0.5f * x0, 0.5f * x1), f2pack(1.f + e0, 1.f + e1));
+}
+
+// 32 bias values for columns [col, col + 32) (zeros past n), the same for every lane: uniform
+// 16-byte loads that the L1 broadcasts, in place of one shuffle per output element.
+__device__ __forceinline__ void load_bias32(const void* bias, int kind, int col, int n, float (&b)[32]) {
+  if (kind == kBiasF32) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (col + 4 * j < n) v = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(bias) + col) + j);
+      b[4 * j] = v.x;
+      b[4 * j + 1] = v.y;
+      b[4 * j + 2] = v.z;
+      b[4 * j + 3] = v.w;
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (col + 8 * j < n)
+      v = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(bias) + col) + j);
+    auto put = [&](uint32_t word, int e) {
+      float lo, hi;
+      if (kind == kBiasBF16)
+        Cvt<__nv_bfloat16>::unpack(word, lo, hi);
+      else
+        Cvt<__half>::unpack(word, lo, hi);
+      b[8 * j + 2 * e] = lo;
+      b[8 * j + 2 * e + 1] = hi;
+    };
+    put(v.x, 0);
+    put(v.y, 1);
+    put(v.z, 2);
+    put(v.w, 3);
+  }
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
@@ -250,20 +299,25 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
       } else {
         uint32_t v[32];
         tmem_ld32(t_row + col0, v);
-        // one bias value per lane, broadcast across the row by shuffles
-        const float bl = load_bias(p.bias, p.bias_kind, col_base + col0 + lane, p.N_out);
-        uint32_t rv[16];  // this lane's row of the residual (read while the TMEM load is in flight)
+        // the bias of these 32 columns (read while the TMEM load is in flight)
+        float bv[32];
+        if (p.bias_kind != kBiasNone) {
+          load_bias32(p.bias, p.bias_kind, col_base + col0, p.N_out, bv);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) bv[i] = 0.f;
+        }
+        uint32_t rv[16];  // this lane's row of the residual
         if (p.resid) load_row32<T>(p.resid, p.resid_ld, row0 + lane, col_base + col0, p.M, p.N_out, rv);
         tmem_wait_ld();
         uint32_t zp[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float x0 = fmaf(__uint_as_float(v[2 * i]), rs, __shfl_sync(0xffffffffu, bl, 2 * i));
-          float x1 = fmaf(__uint_as_float(v[2 * i + 1]), rs, __shfl_sync(0xffffffffu, bl, 2 * i + 1));
+          float x0 = fmaf(__uint_as_float(v[2 * i]), rs, bv[2 * i]);
+          float x1 = fmaf(__uint_as_float(v[2 * i + 1]), rs, bv[2 * i + 1]);
           zp[i] = Cvt<T>::pack(x0, x1);
           if constexpr (EPI == kEpiGelu) {
-            x0 = gelu_erf_epilogue(x0);
-            x1 = gelu_erf_epilogue(x1);
+            f2unpack(gelu_erf_pair(f2pack(x0, x1)), x0, x1);
           } else if constexpr (EPI == kEpiRelu) {
             x0 = fmaxf(x0, 0.f);
             x1 = fmaxf(x1, 0.f);

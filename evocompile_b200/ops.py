@@ -111,6 +111,8 @@ def addmm_act(bias, mat1, mat2, act: int = _lib.ACT_GELU, save_pre: bool = False
             )
         if bias_t.stride(0) != 1:
             bias_t = bias_t.contiguous()
+        if bias_t.data_ptr() % 16:
+            bias_t = bias_t.clone()  # the tensor-core epilogue reads the bias with 16-byte loads
         bias_dt = _lib.dtype_code(bias_t.dtype)
     if out is None:
         out = torch.empty((M, N), device=dev, dtype=mat1.dtype)
