@@ -271,3 +271,14 @@ def test_rowscale_rope_rejects_partial_heads():
     s = torch.ones(8, dtype=torch.float32, device="cuda")
     with pytest.raises(RuntimeError, match="multiple of 128"):
         ops.linear_rowscale(x, w, s, rope=(64, 8, 500000.0))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_p2p_reduction_single_process():
+    """The GEMM epilogue's peer reductions (the fused all-reduce's path without a multicast address)
+    driven from one process: the partial lands in the output on both devices."""
+    from evocompile_b200.tp import p2p_reduction_check
+
+    r = p2p_reduction_check(rows=1000, cols=520, k=264, iters=2)
+    assert r["status"] == 0
+    assert r["rel_err_cuda0"] <= TOL and r["rel_err_cuda1"] <= TOL
