@@ -86,9 +86,10 @@ class ClockSampler:
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, settle_s: float = 0.3):
         self.proc = None
         self.out = None
+        self.settle_s = settle_s
         try:
             uuid = str(torch.cuda.get_device_properties(device_index).uuid)
             sel = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
@@ -100,7 +101,8 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(self.cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            time.sleep(0.3)
+            if self.settle_s > 0:
+                time.sleep(self.settle_s)
         except Exception:
             self.proc = None
         return self
@@ -824,14 +826,16 @@ def _timed_region(wl, steps, warmup, world, local, dev):
     from evocompile_b200 import _lib
 
     stream = torch.cuda.current_stream(dev)
-    _warm(wl.step, warmup, world, dev)
-    if _lib.read_status(dev):
-        raise RuntimeError(f"{wl.name}: kernel timeout during warm-up")
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize(dev)
-    with ClockSampler(local) as clocks:
+    # the clock sampler starts before the warm-up: nvidia-smi's start-up then overlaps GPU work
+    # instead of leaving the GPU idle (and its clocks falling) right before the timed steps
+    with ClockSampler(local, settle_s=0.0) as clocks:
+        _warm(wl.step, warmup, world, dev)
+        if _lib.read_status(dev):
+            raise RuntimeError(f"{wl.name}: kernel timeout during warm-up")
+        barrier(world)
+        torch.cuda.synchronize(dev)
         e0.record(stream)
         for i in range(steps):
             wl.last_out = wl.step(kev[i])
