@@ -206,7 +206,10 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
     // wave of concurrently running tiles (one per SM): sqrt(SMs * 256 / 128) A row-blocks or
     // sqrt(SMs * 128 / 256) B column-blocks (measured +6..17% on K = 28672, neutral at K <= 8192).
 #ifndef GKO_GEMM_L2_GROUP_MB
-#define GKO_GEMM_L2_GROUP_MB 32
+// measured on B200 (sustained, power-capped): 48 MB gave the Llama-3-70B gate/up (16384 x 57344 x
+// 8192) 12.37 ms against 12.79 at 32 MB and 14.3 at 64 MB (the group no longer stays in the 126 MB
+// L2 next to the streamed operand); the 8B MLP and the 70B down / QKV shapes moved by under 2 %
+#define GKO_GEMM_L2_GROUP_MB 48
 #endif
     const double budget = GKO_GEMM_L2_GROUP_MB * 1024.0 * 1024.0;
     const double a_bytes = (double)M * K * esz, b_bytes = (double)nb_total * K * esz;
