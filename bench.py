@@ -595,7 +595,9 @@ class TPBlockWorkload(SwigluMLP):
                                "fused": "inside the GEMM over NVLink (multicast reduction)",
                                "nccl": "NCCL all-reduce after each GEMM",
                                "pipe": f"NCCL all-reduces of {self.block.chunks} token chunks overlapping the "
-                                       f"next chunks' GEMMs"}[self.block.comm]) + ")",
+                                       f"next chunks' GEMMs",
+                               "nvls": "NVSwitch multicast reduction of row slices fused with the residual "
+                                       "add and RMS statistics"}[self.block.comm]) + ")",
             "l2": "weights 1.7 GB / tp, activations > L2; no flush",
         }
 
@@ -1051,7 +1053,7 @@ def main():
                     help=f"comma-separated per-configuration records to add (default: {','.join(SUB_WORKLOADS)})")
     ap.add_argument("--small", action="store_true",
                     help="attention workloads at B=4, H=16 (a capture-sized case for ncu --set full)")
-    ap.add_argument("--tp-comm", choices=("auto", "fused", "nccl", "pipe"), default="auto",
+    ap.add_argument("--tp-comm", choices=("auto", "fused", "nccl", "pipe", "nvls"), default="auto",
                     help="tp_block: sum row-parallel outputs inside the GEMM (fused), with a blocking NCCL "
                          "all-reduce (nccl), with NCCL all-reduces of token chunks overlapping the next "
                          "chunks' GEMMs (pipe), or per rank count (auto)")

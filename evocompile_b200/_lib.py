@@ -98,6 +98,7 @@ SIGNATURES = {
         [_int, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _fl, _vp, _vp],
     ),
     "gko_set_gemm_ctas": (_int, [_int]),
+    "gko_allreduce_residual_nvls": (_int, [_int, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _fl, _vp, _vp]),
     "gko_swiglu_bwd": (_int, [_int, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp]),
     "gko_silu_mul": (_int, [_int, _i64, _vp, _vp, _vp, _vp, _vp]),
     "gko_selftest_wait_timeout": (_int, [_vp, ctypes.c_longlong, _vp]),

@@ -136,15 +136,17 @@ class TPBlock:
     (NCCL) or None for a single GPU.
 
     ``comm``: "fused" sums the row-parallel outputs inside the GEMM over NVLink; "nccl" runs each
-    row-parallel GEMM then a blocking NCCL all-reduce; "pipe" splits the tokens after attention
+    row-parallel GEMM then a blocking NCCL all-reduce; "nvls" writes each row-parallel partial to
+    symmetric memory and sums it in the NVSwitch, each rank reducing a slice of the rows with the
+    residual add and the next RMSNorm's statistics folded in (``tp.NvlsResidualReduce``); "pipe" splits the tokens after attention
     into ``chunks`` and pipelines them (``post_attention_schedule``): each chunk's all-reduces run
     on a communication stream while later chunks' GEMMs run, with the GEMMs capped at all SMs but
     ``comm_sms`` so that NCCL's kernels have SMs of their own; "auto" picks per rank count."""
 
     def __init__(self, local: dict, cfg: BlockConfig, group=None, comm: str = "auto", chunks: int = 4,
                  comm_sms: int = 16):
-        if comm not in ("auto", "fused", "nccl", "pipe"):
-            raise ValueError(f"comm must be 'auto', 'fused', 'nccl' or 'pipe', got {comm!r}")
+        if comm not in ("auto", "fused", "nccl", "pipe", "nvls"):
+            raise ValueError(f"comm must be 'auto', 'fused', 'nccl', 'pipe' or 'nvls', got {comm!r}")
         self.chunks = chunks
         self.comm_sms = comm_sms
         self._comm_stream = None
@@ -188,6 +190,16 @@ class TPBlock:
             self._fused[key] = f
         y = f(x, weight)
         return y if resid is None else resid.add_(y)
+
+    def _nvls(self, slot, rows, cols, dtype, device, stats):
+        from .tp import NvlsResidualReduce
+
+        key = ("nvls", slot, rows, cols, dtype)
+        r = self._fused.get(key)
+        if r is None:  # collective: every rank builds it at the same call
+            r = NvlsResidualReduce(rows, cols, dtype, device, self.group, stats)
+            self._fused[key] = r
+        return r
 
     def _post_attention_pipelined(self, attn2d, x2):
         """o-projection, residual, RMSNorm, SwiGLU MLP and both all-reduces, token chunk by token
@@ -270,6 +282,20 @@ class TPBlock:
         attn = torch.empty(T, hq, hd, device=x.device, dtype=x.dtype)
         ops.fmha_fwd(as4(q), as4(k), as4(v), None, hd ** -0.5, 1, out=as4(attn))
         mk("attention")
+        if self.comm == "nvls" and self.world > 1:
+            x1, inv2 = self._nvls(0, T, d, x.dtype, x.device, True)(attn.view(T, hq * hd), w["wo"], x2, cfg.eps)
+            mk("o_proj")
+            mk("norm2")  # the residual add and the statistics ran inside the reduction
+            if events is not None:
+                events[0].record()
+            g = ops.linear_rowscale(x1, w["w_gate_up_n"], inv2, swiglu=True)
+            if events is not None:
+                events[1].record()
+            mk("gate_up")
+            y, _ = self._nvls(1, T, d, x.dtype, x.device, False)(g, w["w_down"], x1, cfg.eps)
+            y = y.clone().view(B, S, d)  # the symmetric buffer is rewritten by the next call
+            mk("down")
+            return y
         if self.comm == "pipe" and self.world > 1:
             # ``events`` bracket the whole pipelined post-attention part here (its GEMMs and
             # all-reduces interleave, so no single kernel can be bracketed)

@@ -420,6 +420,41 @@ __device__ __forceinline__ void multimem_red_add_x8(void* mc, uint4 v) {
                  : "memory");
 }
 
+// Sum over every GPU bound to the multicast address `mc` of the 8 packed bf16 / f16 values there,
+// accumulated in fp32 inside the switch and returned rounded to the element type (NVLS).
+template <typename T>
+__device__ __forceinline__ uint4 multimem_ld_reduce_add_x8(const void* mc) {
+  uint4 v;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(mc)
+                 : "memory");
+  else
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(mc)
+                 : "memory");
+  return v;
+}
+
+// Store 8 packed bf16 / f16 values to every GPU bound to the multicast address `mc`.
+template <typename T>
+__device__ __forceinline__ void multimem_st_x8(void* mc, uint4 v) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value)
+    asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+  else
+    asm volatile("multimem.st.relaxed.sys.global.v4.f16x2 [%0], {%1, %2, %3, %4};" ::"l"(mc), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ void multimem_st_f32(void* mc, float v) {
+  asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc), "f"(v) : "memory");
+}
+
 // dst[0..8) += v at a (possibly peer, NVLink-mapped) global address.
 template <typename T>
 __device__ __forceinline__ void red_add_x8(void* dst, uint4 v) {

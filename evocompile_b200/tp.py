@@ -17,6 +17,8 @@ on the same stream.
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib, ops
@@ -111,3 +113,59 @@ if __name__ == "__main__":
     ap.add_argument("--iters", type=int, default=5)
     a = ap.parse_args()
     print(json.dumps(p2p_reduction_check(a.rows, a.cols, a.k, a.iters)))
+
+
+class NvlsResidualReduce:
+    """The sum over the group of a row-parallel projection's output, plus a residual (and the
+    RMSNorm statistics of the result), through NVLink multicast (``gko_allreduce_residual_nvls``).
+
+    A call: the GEMM writes this rank's partial into its copy of a symmetric buffer (no
+    communication), group barrier, every rank sums its slice of the rows over all ranks in the
+    switch, adds the residual and writes the rows (and 1/rms per row) to every rank's copy of the
+    output buffers, group barrier. Returns (out, inv) — the symmetric output buffer and the fp32
+    statistics (None without ``stats``), valid until the next call on this object.
+    """
+
+    def __init__(self, rows: int, cols: int, dtype, device, group, stats: bool):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from .shard import row_range
+
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.row0, self.row1 = row_range(rows, self.rank, self.world)
+        self.partial = symm_mem.empty((rows, cols), dtype=dtype, device=device)
+        self.hp = symm_mem.rendezvous(self.partial, group.group_name)
+        self.out = symm_mem.empty((rows, cols), dtype=dtype, device=device)
+        self.ho = symm_mem.rendezvous(self.out, group.group_name)
+        self.inv = self.hi = None
+        if stats:
+            self.inv = symm_mem.empty((rows,), dtype=torch.float32, device=device)
+            self.hi = symm_mem.rendezvous(self.inv, group.group_name)
+        for h in (self.hp, self.ho, self.hi):
+            if h is not None and not int(h.multicast_ptr or 0):
+                raise RuntimeError("NvlsResidualReduce needs NVLink multicast (NVLS) on this group")
+
+    def __call__(self, x: torch.Tensor, weight: torch.Tensor, resid, eps: float = 1e-5):
+        rows, cols = self.partial.shape
+        if tuple(x.shape[:-1]) != (rows,) or weight.shape[0] != cols:
+            raise RuntimeError(f"NvlsResidualReduce built for [{rows}, {cols}], got x {tuple(x.shape)} "
+                               f"weight {tuple(weight.shape)}")
+        if resid is not None and (tuple(resid.shape) != (rows, cols) or resid.stride() != (cols, 1)):
+            raise RuntimeError("NvlsResidualReduce: the residual is a contiguous [rows, cols] tensor")
+        dev = x.device
+        ops.linear(x, weight, out=self.partial)
+        self.hp.barrier(channel=0)
+        with torch.cuda.device(dev):
+            rc = _lib.load().gko_allreduce_residual_nvls(
+                _lib.dtype_code(x.dtype), rows, cols, cols, self.row0, self.row1,
+                ctypes.c_void_p(int(self.hp.multicast_ptr)),
+                ctypes.c_void_p(resid.data_ptr() if resid is not None else 0),
+                ctypes.c_void_p(int(self.ho.multicast_ptr)),
+                ctypes.c_void_p(int(self.hi.multicast_ptr) if self.hi is not None else 0), float(eps),
+                ctypes.c_void_p(_lib.status_word(dev).data_ptr()), ctypes.c_void_p(_lib.stream_ptr(dev)))
+        _lib.check(rc, "gko_allreduce_residual_nvls")
+        self.hp.barrier(channel=0)
+        return self.out, self.inv

@@ -340,6 +340,24 @@ int gko_linear_rowscale_rope(int dtype, int64_t m, int64_t n, int64_t k, const v
 int gko_set_gemm_ctas(int ctas);
 
 /*
+ * Row-slice all-reduce of a tensor-parallel row-parallel projection over NVLink multicast, fused
+ * with the residual add and the RMSNorm statistics that follow it. Every rank has written its
+ * partial [rows, cols] (row stride ld) into its copy of a symmetric buffer whose multicast address
+ * is partial_mc, and the group has passed a barrier. This rank then sums rows [row0, row1) over the
+ * ranks (multimem.ld_reduce, fp32 accumulation in the switch), adds resid (local, same row stride;
+ * NULL: none), and writes the rounded rows to every rank's copy of the output buffer (out_mc) and,
+ * when inv_mc is not NULL, 1 / sqrt(mean(v^2) + eps) of each row to every rank's fp32 [rows]
+ * buffer. A barrier after the call completes the all-reduce on every rank. bf16 / f16, cols and
+ * ld multiples of 8, cols <= 16384.
+ *
+ * No reference counterpart (the reference has no tensor parallelism): it replaces the NCCL
+ * all-reduce after the block's o- and down projections, and the residual / statistics pass.
+ */
+int gko_allreduce_residual_nvls(int dtype, int64_t rows, int64_t cols, int64_t ld, int64_t row0, int64_t row1,
+                                const void* partial_mc, const void* resid, void* out_mc, void* inv_mc, float eps,
+                                unsigned int* status, void* stream);
+
+/*
  * y = rmsnorm(x + residual) * weight over rows of `cols` elements (row stride ld),
  * rmsnorm(v) = v / sqrt(mean(v^2) + eps). residual may be NULL; when sum_out is
  * not NULL it receives x + residual (the updated residual stream). bf16/f16,

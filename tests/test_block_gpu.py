@@ -147,7 +147,7 @@ def _tp_worker(rank, world, port, q, comm="fused"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("comm", ["fused", "nccl"])
+@pytest.mark.parametrize("comm", ["fused", "nccl", "nvls", "pipe"])
 def test_block_tp2(comm):
     import torch.multiprocessing as mp
 
