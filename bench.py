@@ -49,7 +49,9 @@ METRIC = "fused-kernel TFLOP/s"
 # --small: the attention workloads at B=4, H=16 (inputs still > L2), for full ncu captures
 SMALL = False
 # --tp-comm: how the tensor-parallel block sums its row-parallel outputs ("fused": inside the
-# GEMM over NVLink; "nccl": GEMM then NCCL all-reduce; "auto": fused on two ranks, NCCL on more)
+# GEMM over NVLink; "nccl": GEMM then NCCL all-reduce; "nvls": NVSwitch reduction of row slices
+# fused with the residual and statistics; "pipe": token-chunk pipeline of NCCL all-reduces;
+# "auto": fused on two ranks, NCCL on four, NVLS on eight)
 TP_COMM = "auto"
 # --tp-chunks / --tp-comm-sms: token chunks of the pipelined form and the SMs its GEMMs leave free
 TP_CHUNKS = 4

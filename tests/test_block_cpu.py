@@ -85,12 +85,13 @@ def test_tp2_matches_unsharded():
 
 
 def test_comm_auto_policy(monkeypatch):
-    """comm="auto" sums row-parallel outputs inside the GEMM on two ranks and with NCCL on more
-    (the faster form measured at TP2 and TP4); explicit modes are kept; others are rejected."""
+    """comm="auto" sums row-parallel outputs inside the GEMM on two ranks, with NCCL on four and
+    through the NVLS row-slice reduction on eight (the fastest form measured at each); explicit
+    modes are kept; others are rejected."""
     from evocompile_b200.block import TPBlock
 
     local = shard_weights(init_weights(CFG, torch.device("cpu"), torch.float32, seed=1), CFG, 0, 1)
-    for world, want in ((2, "fused"), (4, "nccl"), (8, "nccl")):
+    for world, want in ((2, "fused"), (4, "nccl"), (8, "nvls")):
         monkeypatch.setattr(dist, "get_world_size", lambda group=None, w=world: w)
         assert TPBlock(local, CFG, group=object()).comm == want
         assert TPBlock(local, CFG, group=object(), comm="fused").comm == "fused"
