@@ -51,7 +51,7 @@ SMALL = False
 # --tp-comm: how the tensor-parallel block sums its row-parallel outputs ("fused": inside the
 # GEMM over NVLink; "nccl": GEMM then NCCL all-reduce; "nvls": NVSwitch reduction of row slices
 # fused with the residual and statistics; "pipe": token-chunk pipeline of NCCL all-reduces;
-# "auto": fused on two ranks, NCCL on four, NVLS on eight)
+# "nvls_pipe": token-chunk pipeline of the NVSwitch reductions; "auto": per rank count)
 TP_COMM = "auto"
 # --tp-chunks / --tp-comm-sms: token chunks of the pipelined form and the SMs its GEMMs leave free
 TP_CHUNKS = 4
@@ -579,7 +579,7 @@ class TPBlockWorkload(SwigluMLP):
         self.flop_step = self.cfg.flops(T, self.S)
         ff_l = self.cfg.d_ff // world
         self.flop_gateup = 2.0 * T * self.cfg.d_model * 2 * ff_l
-        if self.block.comm == "pipe" and world > 1:
+        if self.block.comm in ("pipe", "nvls_pipe") and world > 1:
             # the step's events bracket the pipelined post-attention part: o-projection, gate/up
             # and down GEMMs with their all-reduces
             self.dominant = "post_attention_pipelined"
@@ -599,7 +599,10 @@ class TPBlockWorkload(SwigluMLP):
                                "pipe": f"NCCL all-reduces of {self.block.chunks} token chunks overlapping the "
                                        f"next chunks' GEMMs",
                                "nvls": "NVSwitch multicast reduction of row slices fused with the residual "
-                                       "add and RMS statistics"}[self.block.comm]) + ")",
+                                       "add and RMS statistics",
+                               "nvls_pipe": f"NVSwitch reductions (residual add and RMS statistics fused) of "
+                                            f"{self.block.chunks} token chunks overlapping the next chunks' "
+                                            f"GEMMs"}[self.block.comm]) + ")",
             "l2": "weights 1.7 GB / tp, activations > L2; no flush",
         }
 
@@ -1055,12 +1058,14 @@ def main():
                     help=f"comma-separated per-configuration records to add (default: {','.join(SUB_WORKLOADS)})")
     ap.add_argument("--small", action="store_true",
                     help="attention workloads at B=4, H=16 (a capture-sized case for ncu --set full)")
-    ap.add_argument("--tp-comm", choices=("auto", "fused", "nccl", "pipe", "nvls"), default="auto",
+    ap.add_argument("--tp-comm", choices=("auto", "fused", "nccl", "pipe", "nvls", "nvls_pipe"), default="auto",
                     help="tp_block: sum row-parallel outputs inside the GEMM (fused), with a blocking NCCL "
                          "all-reduce (nccl), with NCCL all-reduces of token chunks overlapping the next "
-                         "chunks' GEMMs (pipe), or per rank count (auto)")
-    ap.add_argument("--tp-chunks", type=int, default=4, help="tp_block pipe: token chunks")
-    ap.add_argument("--tp-comm-sms", type=int, default=16, help="tp_block pipe: SMs the GEMMs leave to NCCL")
+                         "chunks' GEMMs (pipe), with NVSwitch reductions of row slices (nvls) or of token "
+                         "chunks overlapping the next chunks' GEMMs (nvls_pipe), or per rank count (auto)")
+    ap.add_argument("--tp-chunks", type=int, default=4, help="tp_block pipe / nvls_pipe: token chunks")
+    ap.add_argument("--tp-comm-sms", type=int, default=16,
+                    help="tp_block pipe / nvls_pipe: SMs the GEMMs leave to the reductions")
     args = ap.parse_args()
     global SMALL, TP_COMM, TP_CHUNKS, TP_COMM_SMS
     SMALL = args.small

@@ -141,12 +141,14 @@ class TPBlock:
     residual add and the next RMSNorm's statistics folded in (``tp.NvlsResidualReduce``); "pipe" splits the tokens after attention
     into ``chunks`` and pipelines them (``post_attention_schedule``): each chunk's all-reduces run
     on a communication stream while later chunks' GEMMs run, with the GEMMs capped at all SMs but
-    ``comm_sms`` so that NCCL's kernels have SMs of their own; "auto" picks per rank count."""
+    ``comm_sms`` so that NCCL's kernels have SMs of their own; "nvls_pipe" is the same token-chunk
+    pipeline with each chunk summed by the NVSwitch reduction of "nvls" instead of NCCL; "auto"
+    picks per rank count."""
 
     def __init__(self, local: dict, cfg: BlockConfig, group=None, comm: str = "auto", chunks: int = 4,
                  comm_sms: int = 16):
-        if comm not in ("auto", "fused", "nccl", "pipe", "nvls"):
-            raise ValueError(f"comm must be 'auto', 'fused', 'nccl', 'pipe' or 'nvls', got {comm!r}")
+        if comm not in ("auto", "fused", "nccl", "pipe", "nvls", "nvls_pipe"):
+            raise ValueError(f"comm must be 'auto', 'fused', 'nccl', 'pipe', 'nvls' or 'nvls_pipe', got {comm!r}")
         self.chunks = chunks
         self.comm_sms = comm_sms
         self._comm_stream = None
@@ -203,6 +205,61 @@ class TPBlock:
             self._fused[key] = r
         return r
 
+    def _comm(self, device):
+        if self._comm_stream is None:
+            self._comm_stream = torch.cuda.Stream(device)
+        return self._comm_stream
+
+    def _post_attention_nvls_pipelined(self, attn2d, x2):
+        """``_post_attention_pipelined`` with each chunk's sums done by the NVSwitch reductions
+        (``tp.NvlsResidualReduce.reduce_rows``): the o-projection and down GEMMs of a chunk write
+        its rows of this rank's partial into symmetric memory on the compute stream; on the
+        communication stream the chunk's rows are summed in the switch with the residual added
+        (and, after the o-projection, the RMSNorm statistics computed) while the next chunks'
+        GEMMs run. Returns the block output [T, d]."""
+        from .shard import row_range
+
+        w, cfg = self.w, self.cfg
+        T, d = x2.shape
+        chunks = max(1, min(self.chunks, T))
+        rng = [row_range(T, c, chunks) for c in range(chunks)]
+        cur = torch.cuda.current_stream()
+        comm = self._comm(x2.device)
+        r_o = self._nvls(0, T, d, x2.dtype, x2.device, True)
+        r_d = self._nvls(1, T, d, x2.dtype, x2.device, False)
+        x1, inv2 = r_o.out, r_o.inv  # summed o-projection + residual, and its 1/rms per row
+        done_o, done_ar, done_mlp = {}, {}, {}
+        comm.wait_stream(cur)
+        sms = torch.cuda.get_device_properties(x2.device).multi_processor_count
+        prev = ops.set_gemm_ctas(max(1, sms - self.comm_sms))
+        try:
+            for kind, c in post_attention_schedule(chunks):
+                a, b = rng[c]
+                if kind == "o":
+                    ops.linear(attn2d[a:b], w["wo"], out=r_o.partial[a:b])
+                    done_o[c] = torch.cuda.Event()
+                    done_o[c].record(cur)
+                elif kind == "ar_o":
+                    comm.wait_event(done_o[c])
+                    with torch.cuda.stream(comm):
+                        r_o.reduce_rows(a, b, x2, cfg.eps)
+                        done_ar[c] = torch.cuda.Event()
+                        done_ar[c].record(comm)
+                elif kind == "mlp":
+                    cur.wait_event(done_ar[c])
+                    g = ops.linear_rowscale(x1[a:b], w["w_gate_up_n"], inv2[a:b], swiglu=True)
+                    ops.linear(g, w["w_down"], out=r_d.partial[a:b])
+                    done_mlp[c] = torch.cuda.Event()
+                    done_mlp[c].record(cur)
+                else:  # "ar_d"
+                    comm.wait_event(done_mlp[c])
+                    with torch.cuda.stream(comm):
+                        r_d.reduce_rows(a, b, x1, cfg.eps)
+        finally:
+            ops.set_gemm_ctas(prev)
+        cur.wait_stream(comm)
+        return r_d.out.clone()  # the symmetric buffer is rewritten by the next call
+
     def _post_attention_pipelined(self, attn2d, x2):
         """o-projection, residual, RMSNorm, SwiGLU MLP and both all-reduces, token chunk by token
         chunk (``post_attention_schedule``); returns the block output [T, d]."""
@@ -213,9 +270,7 @@ class TPBlock:
         chunks = max(1, min(self.chunks, T))
         rng = [row_range(T, c, chunks) for c in range(chunks)]
         cur = torch.cuda.current_stream()
-        if self._comm_stream is None:
-            self._comm_stream = torch.cuda.Stream(x2.device)
-        comm = self._comm_stream
+        comm = self._comm(x2.device)
         rank0 = torch.distributed.get_rank(self.group) == 0
         y = torch.empty(T, d, device=x2.device, dtype=x2.dtype)
         o, x1, done_o, done_ar, done_mlp = {}, {}, {}, {}, {}
@@ -298,12 +353,13 @@ class TPBlock:
             y = y.clone().view(B, S, d)  # the symmetric buffer is rewritten by the next call
             mk("down")
             return y
-        if self.comm == "pipe" and self.world > 1:
+        if self.comm in ("pipe", "nvls_pipe") and self.world > 1:
             # ``events`` bracket the whole pipelined post-attention part here (its GEMMs and
             # all-reduces interleave, so no single kernel can be bracketed)
             if events is not None:
                 events[0].record()
-            y = self._post_attention_pipelined(attn.view(T, hq * hd), x2).view(B, S, d)
+            post = self._post_attention_pipelined if self.comm == "pipe" else self._post_attention_nvls_pipelined
+            y = post(attn.view(T, hq * hd), x2).view(B, S, d)
             if events is not None:
                 events[1].record()
             mk("post_attention")

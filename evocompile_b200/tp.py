@@ -130,12 +130,9 @@ class NvlsResidualReduce:
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm_mem
 
-        from .shard import row_range
-
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
-        self.row0, self.row1 = row_range(rows, self.rank, self.world)
         self.partial = symm_mem.empty((rows, cols), dtype=dtype, device=device)
         self.hp = symm_mem.rendezvous(self.partial, group.group_name)
         self.out = symm_mem.empty((rows, cols), dtype=dtype, device=device)
@@ -153,14 +150,30 @@ class NvlsResidualReduce:
         if tuple(x.shape[:-1]) != (rows,) or weight.shape[0] != cols:
             raise RuntimeError(f"NvlsResidualReduce built for [{rows}, {cols}], got x {tuple(x.shape)} "
                                f"weight {tuple(weight.shape)}")
+        ops.linear(x, weight, out=self.partial)
+        self.reduce_rows(0, rows, resid, eps)
+        return self.out, self.inv
+
+    def reduce_rows(self, a: int, b: int, resid, eps: float = 1e-5) -> None:
+        """Sum rows [a, b) of the partials over the group, on the current stream: barrier (every
+        rank has written those rows of its partial), this rank's slice of [a, b) reduced in the
+        switch (plus the residual's rows, and the statistics) and stored to every rank's copy of
+        the output, barrier (every rank's stores have landed). Rows outside [a, b) are untouched,
+        so consecutive row ranges can be reduced while later rows' partials are still being
+        computed on another stream. ``resid``: the whole contiguous [rows, cols] residual, or None."""
+        from .shard import row_range
+
+        rows, cols = self.partial.shape
+        if not 0 <= a <= b <= rows:
+            raise RuntimeError(f"NvlsResidualReduce: rows [{a}, {b}) outside [0, {rows})")
         if resid is not None and (tuple(resid.shape) != (rows, cols) or resid.stride() != (cols, 1)):
             raise RuntimeError("NvlsResidualReduce: the residual is a contiguous [rows, cols] tensor")
-        dev = x.device
-        ops.linear(x, weight, out=self.partial)
+        r0, r1 = row_range(b - a, self.rank, self.world)
+        dev = self.partial.device
         self.hp.barrier(channel=0)
         with torch.cuda.device(dev):
             rc = _lib.load().gko_allreduce_residual_nvls(
-                _lib.dtype_code(x.dtype), rows, cols, cols, self.row0, self.row1,
+                _lib.dtype_code(self.partial.dtype), rows, cols, cols, a + r0, a + r1,
                 ctypes.c_void_p(int(self.hp.multicast_ptr)),
                 ctypes.c_void_p(resid.data_ptr() if resid is not None else 0),
                 ctypes.c_void_p(int(self.ho.multicast_ptr)),
@@ -168,4 +181,3 @@ class NvlsResidualReduce:
                 ctypes.c_void_p(_lib.status_word(dev).data_ptr()), ctypes.c_void_p(_lib.stream_ptr(dev)))
         _lib.check(rc, "gko_allreduce_residual_nvls")
         self.hp.barrier(channel=0)
-        return self.out, self.inv

@@ -95,6 +95,7 @@ def test_comm_auto_policy(monkeypatch):
         monkeypatch.setattr(dist, "get_world_size", lambda group=None, w=world: w)
         assert TPBlock(local, CFG, group=object()).comm == want
         assert TPBlock(local, CFG, group=object(), comm="fused").comm == "fused"
+        assert TPBlock(local, CFG, group=object(), comm="nvls_pipe").comm == "nvls_pipe"
     import pytest
 
     with pytest.raises(ValueError):
@@ -194,3 +195,23 @@ def test_pipelined_tp2_matches_unsharded():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert err < 1e-5
+
+
+def test_nvls_chunk_slices_partition_rows():
+    """The pipelined NVSwitch form reduces, per token chunk [a, b), the slice
+    a + row_range(b - a, rank, world) on each rank: over all chunks and ranks every row of the
+    block's output is summed exactly once (ragged chunk and rank splits included)."""
+    from evocompile_b200.shard import row_range
+
+    for T in (1, 7, 320, 16384, 16387):
+        for chunks in (1, 3, 4, 7):
+            for world in (2, 4, 8):
+                seen = [0] * T
+                for c in range(max(1, min(chunks, T))):
+                    a, b = row_range(T, c, max(1, min(chunks, T)))
+                    for r in range(world):
+                        r0, r1 = row_range(b - a, r, world)
+                        assert a <= a + r0 <= a + r1 <= b
+                        for i in range(a + r0, a + r1):
+                            seen[i] += 1
+                assert seen == [1] * T, (T, chunks, world)
