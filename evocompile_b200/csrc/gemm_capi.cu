@@ -32,8 +32,8 @@ int bias_kind_of(const void* bias, int bias_dtype) {
 }
 
 template <typename T, int EPI, bool B_MN, bool A_MN = false>
-int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td,
-              const GemmParams& p, cudaStream_t stream) {
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& td, const CUtensorMap& tx0,
+              const CUtensorMap& tx1, const GemmParams& p, cudaStream_t stream) {
   auto kern = gemm::gemm_kernel<T, EPI, B_MN, A_MN>;
   static bool configured[64] = {false};  // per instantiation and device
   int dev = 0;
@@ -46,7 +46,7 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& t
   }
   const int limit = gemm_grid_limit();
   const int grid = p.num_tiles < limit ? p.num_tiles : limit;
-  kern<<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(ta, tb, td, p);
+  kern<<<grid, gemm::kThreads, gemm::kSmemBytes, stream>>>(ta, tb, td, tx0, tx1, p);
   return host::cuda_check(cudaGetLastError(), "gemm kernel launch");
 }
 
@@ -90,24 +90,25 @@ int dispatch_pair(int epi, bool b_mn, const CUtensorMap& ta, const CUtensorMap& 
 
 template <typename T>
 int dispatch_tc(int epi, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb,
-                const CUtensorMap& td, const GemmParams& p, cudaStream_t s, bool a_mn = false) {
+                const CUtensorMap& td, const CUtensorMap& tx0, const CUtensorMap& tx1, const GemmParams& p,
+                cudaStream_t s, bool a_mn = false) {
   if (a_mn)  // MN-major A: plain epilogue only (checked by the caller)
-    return b_mn ? launch_tc<T, kEpiNone, true, true>(ta, tb, td, p, s)
-                : launch_tc<T, kEpiNone, false, true>(ta, tb, td, p, s);
+    return b_mn ? launch_tc<T, kEpiNone, true, true>(ta, tb, td, tx0, tx1, p, s)
+                : launch_tc<T, kEpiNone, false, true>(ta, tb, td, tx0, tx1, p, s);
   if (!b_mn) {
     switch (epi) {
-      case kEpiAllReduce: return launch_tc<T, kEpiAllReduce, false>(ta, tb, td, p, s);
-      case kEpiNone: return launch_tc<T, kEpiNone, false>(ta, tb, td, p, s);
-      case kEpiGelu: return launch_tc<T, kEpiGelu, false>(ta, tb, td, p, s);
-      case kEpiRelu: return launch_tc<T, kEpiRelu, false>(ta, tb, td, p, s);
-      default: return launch_tc<T, kEpiSwiglu, false>(ta, tb, td, p, s);
+      case kEpiAllReduce: return launch_tc<T, kEpiAllReduce, false>(ta, tb, td, tx0, tx1, p, s);
+      case kEpiNone: return launch_tc<T, kEpiNone, false>(ta, tb, td, tx0, tx1, p, s);
+      case kEpiGelu: return launch_tc<T, kEpiGelu, false>(ta, tb, td, tx0, tx1, p, s);
+      case kEpiRelu: return launch_tc<T, kEpiRelu, false>(ta, tb, td, tx0, tx1, p, s);
+      default: return launch_tc<T, kEpiSwiglu, false>(ta, tb, td, tx0, tx1, p, s);
     }
   }
   switch (epi) {
-    case kEpiNone: return launch_tc<T, kEpiNone, true>(ta, tb, td, p, s);
-    case kEpiGelu: return launch_tc<T, kEpiGelu, true>(ta, tb, td, p, s);
-    case kEpiRelu: return launch_tc<T, kEpiRelu, true>(ta, tb, td, p, s);
-    default: return launch_tc<T, kEpiSwiglu, true>(ta, tb, td, p, s);
+    case kEpiNone: return launch_tc<T, kEpiNone, true>(ta, tb, td, tx0, tx1, p, s);
+    case kEpiGelu: return launch_tc<T, kEpiGelu, true>(ta, tb, td, tx0, tx1, p, s);
+    case kEpiRelu: return launch_tc<T, kEpiRelu, true>(ta, tb, td, tx0, tx1, p, s);
+    default: return launch_tc<T, kEpiSwiglu, true>(ta, tb, td, tx0, tx1, p, s);
   }
 }
 
@@ -179,6 +180,19 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
     uint32_t box[2] = {64, 32};
     if (!host::encode_tmap(&td, dtype, 2, d, dims, str, box)) return GKO_ERR_INVALID;
   }
+  // the pre-activation output, stored by TMA like D: [M, N_out] at aux (for SwiGLU the gate
+  // columns) and, for SwiGLU, [M, N_out] at aux + N_out (the up columns; 16-byte aligned since
+  // N_out % 8 == 0). Two views keep a ragged last gate chunk from spilling into the up columns.
+  CUtensorMap tx0 = td, tx1 = td;
+  if (aux) {
+    uint64_t dims[2] = {(uint64_t)N_out, (uint64_t)M};
+    uint64_t str[1] = {(uint64_t)(aux_ld * esz)};
+    uint32_t box[2] = {64, 32};
+    if (!host::encode_tmap(&tx0, dtype, 2, aux, dims, str, box)) return GKO_ERR_INVALID;
+    if (epi == kEpiSwiglu &&
+        !host::encode_tmap(&tx1, dtype, 2, static_cast<const uint8_t*>(aux) + N_out * esz, dims, str, box))
+      return GKO_ERR_INVALID;
+  }
   GemmParams p{};
   p.M = (int)M;
   p.N_out = (int)N_out;
@@ -247,8 +261,8 @@ int run_tc(int dtype, int epi, int64_t M, int64_t N_out, int64_t K, int64_t nb_t
     if (dtype == GKO_BF16) return dispatch_pair<__nv_bfloat16>(epi, b_mn, ta, tb, td, p, stream);
     return dispatch_pair<__half>(epi, b_mn, ta, tb, td, p, stream);
   }
-  if (dtype == GKO_BF16) return dispatch_tc<__nv_bfloat16>(epi, b_mn, ta, tb, td, p, stream, a_mn);
-  return dispatch_tc<__half>(epi, b_mn, ta, tb, td, p, stream, a_mn);
+  if (dtype == GKO_BF16) return dispatch_tc<__nv_bfloat16>(epi, b_mn, ta, tb, td, tx0, tx1, p, stream, a_mn);
+  return dispatch_tc<__half>(epi, b_mn, ta, tb, td, tx0, tx1, p, stream, a_mn);
 }
 
 int run_f32(int epi, int64_t M, int64_t N_out, int64_t K, int64_t up_offset, const float* a,

@@ -192,20 +192,11 @@ __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); 
 
 // Converts this warp's half of one accumulator tile (32 TMEM lanes starting at
 // t_row) into the output: TMEM -> registers -> epilogue math -> 128B-swizzled
-// staging buffer -> TMA store of [32 rows x 64 columns] per chunk. Calls
-// `release()` (on one lane, after the warp's last TMEM read of the tile) so the
-// MMA warp may reuse the accumulator. With p.aux set, each lane also writes its row's
-// pre-activation values (32 per half chunk) to the auxiliary output with 16-byte stores.
-template <typename T>
-__device__ __forceinline__ void store_aux_row(void* aux, int64_t ld, int row, int col, int M, int N,
-                                              const uint32_t (&v)[16]) {
-  if (row >= M) return;
-  T* dst = static_cast<T*>(aux) + (int64_t)row * ld + col;
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-    if (col + 8 * j < N)
-      reinterpret_cast<uint4*>(dst)[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-}
+// staging buffer -> TMA store of [32 rows x 64 columns] per chunk. With p.aux set, the
+// pre-activation of the same chunk (for SwiGLU its gate and its up columns) is then read again
+// from TMEM, staged through the same buffer and TMA-stored through tm_x0 (gate / the only
+// pre-activation) and tm_x1 (up). Calls `release()` (on one lane, after the warp's last TMEM
+// read of the tile) so the MMA warp may reuse the accumulator.
 
 // Reads 32 values of row `row` from column `col` (16-byte loads; zeros past M / N).
 template <typename T>
@@ -226,8 +217,30 @@ __device__ __forceinline__ void load_row32(const void* src, int64_t ld, int row,
     }
 }
 
+// Writes 32 packed values (this lane's row, columns [h * 32, h * 32 + 32) of the chunk) into
+// the 128B-swizzled staging row: 16-byte piece j of row `lane` lives at j ^ (lane & 7).
+__device__ __forceinline__ void stage_row32(uint32_t buf, int lane, int h, const uint32_t (&v)[16]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int piece = h * 4 + j;
+    const uint32_t addr = buf + lane * 128 + ((piece ^ (lane & 7)) << 4);
+    st_shared_v4(addr, v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+}
+
+// TMA store of the staged [32 rows x 64 columns] to (col, row0) through `tm` (lane 0).
+__device__ __forceinline__ void store_staged(const CUtensorMap* tm, uint32_t buf, int col, int row0, int lane) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d_hint(tm, buf, col, row0, l2_policy_evict_first());
+    bulk_commit_group();
+  }
+}
+
 template <typename T, int EPI, typename Release>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtensorMap* tm_d,
+                                              const CUtensorMap* tm_x0, const CUtensorMap* tm_x1,
                                               uint32_t t_row, int row0, int col_base, int half,
                                               uint32_t buf, int lane, Release release) {
   constexpr int kBNOut = block_n_out(EPI);
@@ -261,17 +274,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
           const float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
           const float u0 = __uint_as_float(u[2 * i]), u1 = __uint_as_float(u[2 * i + 1]);
           packed[i] = Cvt<T>::pack(silu(g0) * u0, silu(g1) * u1);
-        }
-        if (p.aux) {
-          uint32_t zg[16], zu[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            zg[i] = Cvt<T>::pack(__uint_as_float(g[2 * i]), __uint_as_float(g[2 * i + 1]));
-            zu[i] = Cvt<T>::pack(__uint_as_float(u[2 * i]), __uint_as_float(u[2 * i + 1]));
-          }
-          const int row = row0 + lane, col = col_base + col0;
-          store_aux_row<T>(p.aux, p.aux_ld, row, col, p.M, p.N_out, zg);
-          store_aux_row<T>(p.aux, p.aux_ld, row, p.N_out + col, p.M, 2 * p.N_out, zu);
         }
       } else if (EPI == kEpiNone && p.rope_cols > 0 && col_base + c * 64 < p.rope_cols) {
         // this chunk is one half of a 128-column head: its partner half is 64 columns away
@@ -310,12 +312,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
         uint32_t rv[16];  // this lane's row of the residual
         if (p.resid) load_row32<T>(p.resid, p.resid_ld, row0 + lane, col_base + col0, p.M, p.N_out, rv);
         tmem_wait_ld();
-        uint32_t zp[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           float x0 = fmaf(__uint_as_float(v[2 * i]), rs, bv[2 * i]);
           float x1 = fmaf(__uint_as_float(v[2 * i + 1]), rs, bv[2 * i + 1]);
-          zp[i] = Cvt<T>::pack(x0, x1);
           if constexpr (EPI == kEpiGelu) {
             f2unpack(gelu_erf_pair(f2pack(x0, x1)), x0, x1);
           } else if constexpr (EPI == kEpiRelu) {
@@ -330,17 +330,12 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
           }
           packed[i] = Cvt<T>::pack(x0, x1);
         }
-        if (p.aux) store_aux_row<T>(p.aux, p.aux_ld, row0 + lane, col_base + col0, p.M, p.N_out, zp);
       }
-      // 128B-swizzled staging row: 16-byte piece j of row `lane` lives at j ^ (lane & 7).
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int piece = h * 4 + j;
-        const uint32_t addr = buf + lane * 128 + ((piece ^ (lane & 7)) << 4);
-        st_shared_v4(addr, packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-      }
+      stage_row32(buf, lane, h, packed);
     }
-    if (cc == kMyChunks - 1) {
+    // with a pre-activation output the accumulator is read again below, so it is released
+    // after those reads
+    if (cc == kMyChunks - 1 && !p.aux) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) release();
@@ -365,11 +360,42 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
       }
       __syncwarp();
     } else {
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        tma_store_2d_hint(tm_d, buf, col_base + c * 64, row0, l2_policy_evict_first());
-        bulk_commit_group();
+      store_staged(tm_d, buf, col_base + c * 64, row0, lane);
+      if (p.aux) {
+        // the pre-activation of this chunk, one staged [32 x 64] box per part (SwiGLU: gate, up)
+        constexpr int kParts = EPI == kEpiSwiglu ? 2 : 1;
+#pragma unroll 1
+        for (int part = 0; part < kParts; ++part) {
+          if (lane == 0) bulk_wait_group_read<0>();  // the previous store has read the buffer
+          __syncwarp();
+          const float rs = (p.row_scale && row0 + lane < p.M) ? __ldg(p.row_scale + row0 + lane) : 1.f;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int col0 = c * 64 + h * 32;
+            uint32_t v[32];
+            tmem_ld32(t_row + part * 128 + col0, v);
+            float bv[32];
+            if (EPI != kEpiSwiglu && p.bias_kind != kBiasNone) {
+              load_bias32(p.bias, p.bias_kind, col_base + col0, p.N_out, bv);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) bv[i] = 0.f;
+            }
+            tmem_wait_ld();
+            uint32_t z[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              z[i] = Cvt<T>::pack(fmaf(__uint_as_float(v[2 * i]), rs, bv[2 * i]),
+                                  fmaf(__uint_as_float(v[2 * i + 1]), rs, bv[2 * i + 1]));
+            stage_row32(buf, lane, h, z);
+          }
+          store_staged(part ? tm_x1 : tm_x0, buf, col_base + c * 64, row0, lane);
+        }
+        if (cc == kMyChunks - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) release();
+        }
       }
     }
   }
@@ -381,7 +407,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const CUtenso
 template <typename T, int EPI, bool B_MN, bool A_MN = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                const __grid_constant__ CUtensorMap tm_d, const GemmParams p) {
+                const __grid_constant__ CUtensorMap tm_d, const __grid_constant__ CUtensorMap tm_x0,
+                const __grid_constant__ CUtensorMap tm_x1, const GemmParams p) {
   constexpr int kBNOut = block_n_out(EPI);
   constexpr uint32_t kIdesc =
       make_idesc_f16(std::is_same<T, __nv_bfloat16>::value, kBM, kMmaN, A_MN, B_MN);
@@ -422,6 +449,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tm_a);
     prefetch_tmap(&tm_b);
     prefetch_tmap(&tm_d);
+    if (p.aux) {
+      prefetch_tmap(&tm_x0);
+      if (EPI == kEpiSwiglu) prefetch_tmap(&tm_x1);
+    }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -560,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t_row = tmem_base + acc * kMmaN + (static_cast<uint32_t>(quarter * 32) << 16);
       const int row0 = mb * kBM + quarter * 32;
       const int col_base = nb * kBNOut;
-      epilogue_tile<T, EPI>(p, &tm_d, t_row, row0, col_base, half, buf, lane,
+      epilogue_tile<T, EPI>(p, &tm_d, &tm_x0, &tm_x1, t_row, row0, col_base, half, buf, lane,
                             [&] { mbar_arrive(bar_tempty + 8 * acc); });
     }
     if (lane == 0) bulk_wait_group<0>();
@@ -770,7 +801,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t t_row = tmem_base + acc * kMmaN + (static_cast<uint32_t>(quarter * 32) << 16);
       const int row0 = mb * 2 * kBM + (int)rank * kBM + quarter * 32;
       const uint32_t tempty_leader = mapa_shared(bar_tempty + 8 * acc, 0);
-      epilogue_tile<T, EPI>(p, &tm_d, t_row, row0, nb * kBNOut, half, buf, lane,
+      // the pair path never writes a pre-activation (the host keeps aux launches single-CTA)
+      epilogue_tile<T, EPI>(p, &tm_d, &tm_d, &tm_d, t_row, row0, nb * kBNOut, half, buf, lane,
                             [&] { mbar_arrive_cluster(tempty_leader); });
     }
     if (lane == 0) bulk_wait_group<0>();

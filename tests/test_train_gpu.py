@@ -69,6 +69,32 @@ def test_gemm_swiglu_aux_forward(lead):
     assert oracle.rel_err(gu, ref_gu) <= TOL
 
 
+def test_aux_outputs_many_tiles():
+    """512 output tiles on at most 148 persistent CTAs, so every CTA converts several tiles and
+    reuses its staging buffer and both accumulators: the GELU pre-activation equals the plain
+    (no activation) GEMM bit for bit (same accumulation, same bias add), and the SwiGLU
+    gate / up pre-activations match an fp32 GEMM."""
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(21)
+    M, K, N = 4096, 256, 4096
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=dev, generator=g) * K ** -0.5).to(torch.bfloat16)
+    b = (torch.randn(N, device=dev, generator=g) * 0.1).to(torch.bfloat16)
+    out, z = ops.addmm_act(b, x, w.t(), _lib.ACT_GELU, save_pre=True)
+    plain = ops.addmm_act(b, x, w.t(), _lib.ACT_GELU)
+    pre = ops.addmm_act(b, x, w.t(), _lib.ACT_NONE)
+    H = 2048
+    y, gu = ops.linear_swiglu(x, w, save_pre=True)  # w = [Wg; Wu], H = N / 2
+    torch.cuda.synchronize()
+    assert _lib.read_status(dev) == 0
+    assert torch.equal(out, plain)
+    assert torch.equal(z, pre)
+    ref = x.float() @ w.float().t()
+    assert gu.shape == (M, 2 * H)
+    assert oracle.rel_err(gu.cpu(), ref.cpu()) <= 1e-2
+    assert torch.equal(y, ops.linear_swiglu(x, w))
+
+
 def test_swiglu_bwd_kernel():
     g = torch.Generator().manual_seed(5)
     R, H = 333, 136
