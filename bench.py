@@ -428,12 +428,17 @@ class SwigluTrain(SwigluMLP):
         return self.xg.grad
 
     def step(self, ev=None):
+        # the events bracket the forward gate/up kernel (the record's dominant kernel: it also
+        # writes the pre-activation); the backward launches follow outside them
+        self.xg.grad = None
+        self.wg.grad = None
         if ev is not None:
             ev[0].record()
-        out = self._fwd_bwd(self.api.apply_train)
+        y = self.api.apply_train(self.xg, self.wg)
         if ev is not None:
             ev[1].record()
-        return out
+        y.backward(self.dy)
+        return self.xg.grad
 
     def e2e_setup(self):
         api = self.api
@@ -812,6 +817,12 @@ def run_reference(args):
     return 0
 
 
+# seconds of warm-up work before a timed region: a record starts after the host-only CPU leg
+# of the previous one, and under the 1 kW power cap the SM clock needs some seconds of load to
+# settle (the clocks the sampler saw are in each record's ``clocks``)
+WARM_S = 3.0
+
+
 def _warm(step, warmup, world, dev, min_s=1.0):
     """W warm-up steps, then more until about ``min_s`` seconds of work have run (after a stretch
     of host-only work the GPU's clocks take a while to come back up). Every rank runs the same
@@ -838,7 +849,7 @@ def _timed_region(wl, steps, warmup, world, local, dev):
     # the clock sampler starts before the warm-up: nvidia-smi's start-up then overlaps GPU work
     # instead of leaving the GPU idle (and its clocks falling) right before the timed steps
     with ClockSampler(local, settle_s=0.0) as clocks:
-        _warm(wl.step, warmup, world, dev)
+        _warm(wl.step, warmup, world, dev, min_s=WARM_S)
         if _lib.read_status(dev):
             raise RuntimeError(f"{wl.name}: kernel timeout during warm-up")
         barrier(world)
@@ -989,7 +1000,7 @@ def measure(wl, args, world, rank, local, dev, compare, cpu, cpu_budget_s=10.0):
 
 # the per-configuration records added to the default line: every configuration of the
 # operators at its full size (sharded at N > 1 as the configuration shards)
-SUB_WORKLOADS = ("addmm_gelu", "fmha_causal", "fmha_varlen", "fmha_bwd", "tp_block")
+SUB_WORKLOADS = ("addmm_gelu", "swiglu_train", "fmha_causal", "fmha_varlen", "fmha_bwd", "tp_block")
 
 
 def run_ours(args):
