@@ -584,6 +584,8 @@ class TPBlockWorkload(SwigluMLP):
         self.flop_step = self.cfg.flops(T, self.S)
         ff_l = self.cfg.d_ff // world
         self.flop_gateup = 2.0 * T * self.cfg.d_model * 2 * ff_l
+        if world > 1:
+            self.traffic_key = None  # the captured shape is TP1's; a rank's gate/up is 1/world of it
         if self.block.comm in ("pipe", "nvls_pipe") and world > 1:
             # the step's events bracket the pipelined post-attention part: o-projection, gate/up
             # and down GEMMs with their all-reduces
