@@ -101,3 +101,35 @@ def test_silu_mul_validation(lib):
     assert lib.gko_silu_mul(_lib.BF16, -3, _null(), _null(), _null(), _null(), _null()) == _lib.ERR_INVALID
     assert lib.gko_silu_mul(_lib.BF16, 0, _null(), _null(), _null(), _null(), _null()) == _lib.OK
     assert lib.gko_silu_mul(_lib.BF16, 8, _null(), _null(), _null(), _null(), _null()) == _lib.ERR_INVALID
+
+
+def test_allreduce_residual_nvls_validation(lib):
+    """The NVSwitch row-slice reduction refuses bad arguments on the host, before any launch; an
+    empty row range is a no-op."""
+    def call(dtype=_lib.BF16, rows=64, cols=512, ld=512, r0=0, r1=32, part=16, res=0, out=16, inv=0):
+        return lib.gko_allreduce_residual_nvls(dtype, rows, cols, ld, r0, r1, ctypes.c_void_p(part),
+                                               ctypes.c_void_p(res), ctypes.c_void_p(out), ctypes.c_void_p(inv),
+                                               1e-5, _null(), _null())
+
+    assert call(dtype=_lib.F32) == _lib.ERR_UNSUPPORTED and "bf16 or f16" in _lib.last_error()
+    assert call(r1=65) == _lib.ERR_INVALID and "bad sizes" in _lib.last_error()
+    assert call(r0=10, r1=5) == _lib.ERR_INVALID
+    assert call(ld=256) == _lib.ERR_INVALID
+    assert call(cols=100, ld=104) == _lib.ERR_UNSUPPORTED and "cols % 8" in _lib.last_error()
+    assert call(cols=16392, ld=16392) == _lib.ERR_UNSUPPORTED
+    assert call(r0=7, r1=7) == _lib.OK  # nothing to reduce: no launch, no CUDA call
+    assert call(part=0) == _lib.ERR_INVALID and "multicast" in _lib.last_error()
+    assert call(part=8) == _lib.ERR_UNSUPPORTED and "16-byte" in _lib.last_error()
+    assert call(inv=18) == _lib.ERR_UNSUPPORTED
+
+
+def test_gemm_cta_cap_setter(lib):
+    """gko_set_gemm_ctas returns the previous cap (0 = every SM) and refuses negative values."""
+    prev = lib.gko_set_gemm_ctas(5)
+    try:
+        assert prev == 0
+        assert lib.gko_set_gemm_ctas(9) == 5
+        assert lib.gko_set_gemm_ctas(-1) == -1 and ">= 0" in _lib.last_error()
+        assert lib.gko_set_gemm_ctas(9) == 9
+    finally:
+        lib.gko_set_gemm_ctas(prev)
