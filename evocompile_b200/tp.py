@@ -166,10 +166,12 @@ class NvlsResidualReduce:
         rows, cols = self.partial.shape
         if not 0 <= a <= b <= rows:
             raise RuntimeError(f"NvlsResidualReduce: rows [{a}, {b}) outside [0, {rows})")
-        if resid is not None and (tuple(resid.shape) != (rows, cols) or resid.stride() != (cols, 1)):
-            raise RuntimeError("NvlsResidualReduce: the residual is a contiguous [rows, cols] tensor")
-        r0, r1 = row_range(b - a, self.rank, self.world)
         dev = self.partial.device
+        if resid is not None and (tuple(resid.shape) != (rows, cols) or resid.stride() != (cols, 1)
+                                  or resid.dtype != self.partial.dtype or resid.device != dev):
+            raise RuntimeError("NvlsResidualReduce: the residual is a contiguous [rows, cols] tensor of the "
+                               "output's dtype on the same device")
+        r0, r1 = row_range(b - a, self.rank, self.world)
         self.hp.barrier(channel=0)
         with torch.cuda.device(dev):
             rc = _lib.load().gko_allreduce_residual_nvls(
