@@ -6,8 +6,6 @@ import ctypes
 import re
 from pathlib import Path
 
-import pytest
-
 from evocompile_b200 import _lib
 
 HEADER = Path(__file__).resolve().parents[1] / "include" / "gko_b200.h"

@@ -5,8 +5,6 @@ cover everything a multi-GPU run does outside the kernels)."""
 import os
 import random
 
-import pytest
-import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
