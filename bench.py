@@ -823,6 +823,9 @@ def run_reference(args):
 # of the previous one, and under the 1 kW power cap the SM clock needs some seconds of load to
 # settle (the clocks the sampler saw are in each record's ``clocks``)
 WARM_S = 3.0
+# seconds of continuous warm-up of each comparator arm (torch eager, torch.compile, our step again)
+# right before its timed steps
+COMPARATOR_WARM_S = 2.0
 
 
 def _warm(step, warmup, world, dev, min_s=1.0):
@@ -902,9 +905,11 @@ def _e2e_record(wl, steps, warmup, world, dev, scale):
 
 
 def _comparators(wl, steps, dev):
-    """torch eager and torch.compile of the harness-equivalent module on the same GPU, timed like
-    our arm (K steps, CUDA events), two alternating rounds with our step repeated between them;
-    best round per arm."""
+    """torch eager and torch.compile of the harness-equivalent module on the same GPU, and our
+    step again (``gko_repeat``), each timed like our arm: COMPARATOR_WARM_S seconds of its own
+    continuous warm-up, then K steps between CUDA events. Under the power cap a short burst after
+    other work runs at higher clocks than sustained load, so every arm is measured sustained, as
+    the record's ``value`` is."""
     stream = torch.cuda.current_stream(dev)
     comparators = {}
     fn, fargs = wl.torch_reference()
@@ -920,7 +925,6 @@ def _comparators(wl, steps, dev):
     arms["gko_repeat"] = lambda: wl.step()
     if hasattr(wl, "extra_arms"):
         arms.update(wl.extra_arms())
-    best = {}
     for name, f in list(arms.items()):
         try:
             for _ in range(3):
@@ -929,18 +933,16 @@ def _comparators(wl, steps, dev):
         except Exception as e:  # noqa: BLE001
             comparators[name] = {"error": repr(e)[:200]}
             arms.pop(name)
-    for _ in range(2):
-        for name, f in arms.items():
-            x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            x0.record(stream)
-            for _ in range(steps):
-                f()
-            x1.record(stream)
-            torch.cuda.synchronize(dev)
-            t = x0.elapsed_time(x1) / steps
-            best[name] = min(best.get(name, t), t)
-    for name, t in best.items():
-        comparators[name] = {"ms_per_step": t, "tflops": wl.flop_step / t / 1e9}
+    for name, f in arms.items():
+        _warm(f, 3, 1, dev, min_s=COMPARATOR_WARM_S)
+        x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        x0.record(stream)
+        for _ in range(steps):
+            f()
+        x1.record(stream)
+        torch.cuda.synchronize(dev)
+        t = x0.elapsed_time(x1) / steps
+        comparators[name] = {"ms_per_step": t, "tflops": wl.flop_step / t / 1e9, "warm_s": COMPARATOR_WARM_S}
     torch._dynamo.reset()
     return comparators
 
